@@ -1,0 +1,569 @@
+#!/usr/bin/env python
+"""Throughput benchmark of the sm_100a per-token layer operators.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload chain|add_rms_norm|rms_norm_f32|rope|swiglu|embedding]
+
+Default workload ("chain"): the chained layer-op pass on 65536 tokens per GPU
+-- embedding [32000 x 2048] ~ N(0, 0.02) gathered for ids ~ U[0, 32000) and
+RMSNorm'd (fused), RoPE on Q/K [16, 16, 4096, 128] with a fp32 cos/sin table,
+residual add + RMSNorm [65536 x 2048], SwiGLU [65536 x 5632] ~ 0.5 N(0, 1);
+norm weights 1 + 0.1 N(0, 1), eps 1e-5, scale sqrt(2048), theta 1e4.  Inputs
+are synthetic (seeded), generated on the device.  A step is one pass over
+the rank's 65536 tokens; rows (tokens) are independent, so N GPUs run N
+disjoint shards of an N x 65536-token job with no collective on the data
+path (weak scaling).
+
+The metric is algorithmic HBM GB/s: the bytes the pass must move per token
+(70,660 B: ids, gathered rows, n1, Q/K read+write, o, r, n2, gate/up, y --
+every intermediate that has to reach HBM in the fused minimum) x tokens /
+time.  Every step moves 4.6 GB, far more than the 126 MB L2, so no flush is
+needed between steps.
+
+One JSON line on rank 0 carries: value (device-resident, CUDA events, max
+over ranks), e2e (pinned host buffers -> device -> host through the public
+API, copies overlapped with the kernels), the roofline of the dominant
+kernel (SwiGLU), per-kernel times, the 64-token decode-shape latency (CUDA
+graph), the clocks sampled during the timed region and the oracle's
+multithreaded CPU throughput on a bounded sample.
+
+--impl reference times the reference's path on the CPU (the oracle: a C
+restatement of the reference kernels, all host threads) on the same metric.
+"""
+
+import argparse
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "hrm-text-cuda_b200"))
+
+METRIC = "fused layer-op HBM GB/s (% of B200 peak) and rows/s at 1/2/4/8 GPUs"
+L2_BYTES = 126 * 1000 * 1000
+
+# chain shape (per GPU)
+HIDDEN, HEADS, HEAD_DIM, INTER, VOCAB = 2048, 16, 128, 5632, 32000
+CHAIN_B, CHAIN_S = 16, 4096               # Q/K [16, 16, 4096, 128] -> 65536 tokens
+DECODE_B = 64                             # decode shape: 64 tokens, seq 1, offset 4095
+EPS, THETA = 1e-5, 10000.0
+SCALE = 45.254833995939045                # (float)sqrt(2048)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="chain",
+                    choices=["chain", "add_rms_norm", "rms_norm_f32", "rope", "swiglu", "embedding"])
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-oracle baseline leg")
+    return ap.parse_args()
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def load_traffic(kernel, workload):
+    """dram bytes per launch from the committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    try:
+        text = open(path).read()
+    except OSError:
+        return None
+    m = re.search(rf"^{workload}\s+{kernel}\s+dram_bytes_per_launch=(\d+)", text, re.M)
+    return int(m.group(1)) if m else None
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons via NVML while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, torch_device):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(torch_device).uuid)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.nvml = pynvml
+        except Exception as e:  # noqa: BLE001 - clocks are reported as unavailable
+            self.nvml, self.error = None, f"{type(e).__name__}: {e}"
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM))
+                get = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    n.nvmlDeviceGetCurrentClocksThrottleReasons
+                bits = get(self.h)
+                self.reasons |= {name for b, name in self.REASONS.items() if bits & b}
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.005)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if self.nvml is None:
+            return {"unavailable": self.error}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- workloads
+def randn_bf16(shape, gen, device, std=1.0, mean=0.0):
+    import torch
+
+    x = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
+    if std != 1.0:
+        x.mul_(std)
+    if mean != 0.0:
+        x.add_(mean)
+    return x.to(torch.bfloat16)
+
+
+class Chain:
+    """Chained pass on 65536 tokens per GPU (the default workload)."""
+
+    name = "chain"
+    dominant = "swiglu_ffn"
+
+    def __init__(self, device, rank):
+        import torch
+
+        from hrm_layer_ops import chain, ops
+
+        self.torch, self.chain, self.ops, self.device = torch, chain, ops, device
+        T = CHAIN_B * CHAIN_S
+        self.tokens = T
+        wgen = torch.Generator(device=device).manual_seed(1234)          # weights: same on every rank
+        gen = torch.Generator(device=device).manual_seed(1000 + rank)   # activations: this rank's shard
+        self.w = chain.ChainWeights(
+            table=randn_bf16((VOCAB, HIDDEN), wgen, device, 0.02), w1=randn_bf16(HIDDEN, wgen, device, 0.1, 1.0),
+            w2=randn_bf16(HIDDEN, wgen, device, 0.1, 1.0), rope=ops.rope_table(CHAIN_S, HEAD_DIM, THETA, device),
+            scale=SCALE, eps=EPS, theta=THETA)
+        self.ids = torch.randint(0, VOCAB, (T,), generator=gen, device=device, dtype=torch.int32)
+        self.q = randn_bf16((CHAIN_B, HEADS, CHAIN_S, HEAD_DIM), gen, device)
+        self.k = randn_bf16((CHAIN_B, HEADS, CHAIN_S, HEAD_DIM), gen, device)
+        self.o = randn_bf16((T, HIDDEN), gen, device)
+        self.gate = randn_bf16((T, INTER), gen, device, 0.5)
+        self.up = randn_bf16((T, INTER), gen, device, 0.5)
+        e = torch.empty
+        bf = dict(dtype=torch.bfloat16, device=device)
+        self.h, self.n1, self.r, self.n2 = (e((T, HIDDEN), **bf) for _ in range(4))
+        self.y = e((T, INTER), **bf)
+        per = chain.algorithmic_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)
+        self.per_token = per
+        self.bytes_per_step = per["minimal"] * T
+        self.rows_per_step = T
+        self.kernels = list(chain.CHAIN_KERNELS)
+        self.kernel_bytes = {k: per[k] * T for k in self.kernels}
+        self.footprint = per["op_sum"] * T
+        self.config = {"workload": "chain: embed+RMSNorm -> RoPE -> add+RMSNorm -> SwiGLU",
+                       "tokens_per_gpu": T, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM,
+                       "intermediate": INTER, "vocab": VOCAB, "qk_layout": [CHAIN_B, HEADS, CHAIN_S, HEAD_DIM],
+                       "bytes_per_token_minimal": per["minimal"], "bytes_per_token_moved": per["op_sum"],
+                       "l2": "inputs larger than L2 (4.6 GB moved per step vs 126 MB L2); no flush"}
+
+    def step(self, stream=None, events=None):
+        self.chain.run_device(self.w, self.ids, self.q, self.k, self.o, self.gate, self.up, self.h, self.n1,
+                              self.r, self.n2, self.y, 0, stream=stream, events=events)
+        return len(self.kernels)
+
+    # -- decode shape (64 tokens, offset 4095), launch-latency bound: CUDA graph
+    def decode_latency_us(self, iters=200):
+        torch = self.torch
+        T = DECODE_B
+        dq = self.q[:1, :, :DECODE_B].reshape(DECODE_B, HEADS, 1, HEAD_DIM).clone()  # [64, 16, 1, 128]
+        dk = dq.clone()
+        args = (self.ids[:T], dq, dk, self.o[:T], self.gate[:T], self.up[:T], self.h[:T], self.n1[:T],
+                self.r[:T], self.n2[:T], self.y[:T])
+        s = torch.cuda.Stream(self.device)
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                self.chain.run_device(self.w, *args, 4095, stream=s)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.chain.run_device(self.w, *args, 4095, stream=s)
+        for _ in range(10):
+            g.replay()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(iters):
+            g.replay()
+        t1.record()
+        torch.cuda.synchronize()
+        us = t0.elapsed_time(t1) * 1000.0 / iters
+        del g
+        return us
+
+    # -- end to end: pinned host buffers through the public API
+    def e2e(self, steps):
+        torch = self.torch
+        hc = self.chain.HostChain(self.w, CHAIN_B, HEADS, CHAIN_S, HEAD_DIM, HIDDEN, INTER, chunk_batches=1,
+                                  device=self.device)
+        pin = dict(pin_memory=True)
+        host_in = {n: torch.empty(getattr(self, n).shape, dtype=getattr(self, n).dtype, **pin)
+                   for n in hc.IN}
+        for n in hc.IN:
+            host_in[n].copy_(getattr(self, n))
+        host_out = {n: torch.empty(getattr(self, n).shape, dtype=getattr(self, n).dtype, **pin)
+                    for n in ("q", "k", "h", "n1", "r", "n2", "y")}
+        h2d, d2h = hc.bytes_per_pass(host_in, host_out)
+        hc.run(host_in, host_out)  # warm-up
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches = 0
+        t0.record()
+        for _ in range(steps):
+            launches += hc.run(host_in, host_out)
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / steps
+        return ms, h2d, d2h, launches
+
+    # -- the oracle on a bounded sample of the same pass (one Q/K batch = 4096 tokens)
+    @staticmethod
+    def cpu_sample(min_seconds=8.0, max_reps=50):
+        c = CpuChain()
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            c.run_once()
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= min_seconds or reps >= max_reps:
+                break
+        sec = el / reps
+        return {"gbs": c.bytes / sec / 1e9, "sec_per_sample": sec, "cores": c.cores,
+                "sample": f"{c.tokens} tokens of the chain (one Q/K batch [1, 16, 4096, 128]), {reps} reps, "
+                          f"oracle with {c.cores} OpenMP threads"}
+
+
+class CpuChain:
+    """The chained pass on the host through the oracle (the reference's path,
+    restated in C), on a bounded sample: one Q/K batch of 4096 tokens."""
+
+    def __init__(self):
+        import numpy as np
+
+        sys.path.insert(0, ROOT)
+        from oracle import Oracle, f32_to_bf16
+        from hrm_layer_ops.chain import algorithmic_bytes_per_token
+
+        self.o = o = Oracle()
+        rng = np.random.default_rng(0)
+        self.tokens = T = CHAIN_S
+
+        def nb(shape, std=1.0, mean=0.0):
+            return f32_to_bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(std) + np.float32(mean))
+
+        self.table = nb((VOCAB, HIDDEN), 0.02)
+        self.w1, self.w2 = nb(HIDDEN, 0.1, 1.0), nb(HIDDEN, 0.1, 1.0)
+        self.rope = o.rope_table(CHAIN_S, HEAD_DIM, THETA)
+        self.ids = rng.integers(0, VOCAB, T, dtype=np.uint32)
+        self.q, self.k = nb((1, HEADS, CHAIN_S, HEAD_DIM)), nb((1, HEADS, CHAIN_S, HEAD_DIM))
+        self.ob = nb((T, HIDDEN))
+        self.g, self.u = nb((T, INTER), 0.5), nb((T, INTER), 0.5)
+        self.bytes = algorithmic_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)["minimal"] * T
+        self.cores = o.max_threads()
+
+    def run_once(self):
+        o = self.o
+        h, _ = o.embed_rms_norm(self.ids, self.table, SCALE, self.w1, EPS)
+        o.rope_embed(self.q, self.k, 0, THETA, self.rope)
+        o.add_rms_norm(h, self.ob, self.w2, EPS)
+        o.swiglu_ffn(self.g, self.u)
+
+
+class SingleOp:
+    """One of the per-op workloads (the other layer-op configurations)."""
+
+    def __init__(self, name, device, rank):
+        import torch
+
+        import hrm_layer_ops as ops
+
+        self.torch, self.ops, self.device, self.name = torch, ops, device, name
+        gen = torch.Generator(device=device).manual_seed(2000 + rank)
+        bf = torch.bfloat16
+        if name == "add_rms_norm":        # [16384 x 2048] bf16, weight, eps 1e-5
+            R = 16384
+            self.w = randn_bf16(HIDDEN, gen, device, 0.1, 1.0)
+            self.bytes_per_step, self.rows_per_step = R * HIDDEN * 8, R
+            mk = lambda: (randn_bf16((R, HIDDEN), gen, device), randn_bf16((R, HIDDEN), gen, device),
+                          torch.empty((R, HIDDEN), dtype=bf, device=device),
+                          torch.empty((R, HIDDEN), dtype=bf, device=device))
+            self.cfg = {"workload": "fused residual add + RMSNorm bf16 [16384 x 2048]", "rows": R}
+        elif name == "rms_norm_f32":      # [4096 x 2048] fp32, weight, eps 1e-5
+            R = 4096
+            self.w = torch.randn(HIDDEN, generator=gen, device=device) * 0.1 + 1
+            self.bytes_per_step, self.rows_per_step = R * HIDDEN * 8, R
+            mk = lambda: (torch.randn((R, HIDDEN), generator=gen, device=device),
+                          torch.empty((R, HIDDEN), device=device))
+            self.cfg = {"workload": "RMSNorm fp32 [4096 x 2048]", "rows": R}
+        elif name == "rope":              # Q, K [8, 16, 4096, 128], table
+            shape = (8, HEADS, 4096, HEAD_DIM)
+            self.table = ops.rope_table(4096, HEAD_DIM, THETA, device)
+            self.bytes_per_step, self.rows_per_step = 4 * 2 * 8 * HEADS * 4096 * HEAD_DIM, 8 * 4096
+            mk = lambda: (randn_bf16(shape, gen, device), randn_bf16(shape, gen, device))
+            self.cfg = {"workload": "RoPE Q/K [8, 16, 4096, 128] bf16, fp32 table", "tokens": 8 * 4096}
+        elif name == "swiglu":            # gate, up [32768 x 5632]
+            shape = (32768, INTER)
+            self.bytes_per_step, self.rows_per_step = 32768 * INTER * 6, 32768
+            mk = lambda: (randn_bf16(shape, gen, device, 0.5), randn_bf16(shape, gen, device, 0.5),
+                          torch.empty(shape, dtype=bf, device=device))
+            self.cfg = {"workload": "SwiGLU bf16 [32768 x 5632]", "rows": 32768}
+        elif name == "embedding":         # table [32000 x 2048], 65536 ids
+            T = 65536
+            self.tab = randn_bf16((VOCAB, HIDDEN), gen, device, 0.02)
+            self.bytes_per_step, self.rows_per_step = T * (4 + 2 * 2 * HIDDEN), T
+            mk = lambda: (torch.randint(0, VOCAB, (T,), generator=gen, device=device, dtype=torch.int32),
+                          torch.empty((T, HIDDEN), dtype=bf, device=device))
+            self.cfg = {"workload": "embedding gather [32000 x 2048] table, 65536 ids", "tokens": T}
+        else:
+            raise ValueError(name)
+        # Rotate input sets so that their total exceeds 3x L2: no step finds its inputs in L2.
+        nbuf = max(1, -(-3 * L2_BYTES // self.bytes_per_step))
+        self.bufs = [mk() for _ in range(nbuf)]
+        self.i = 0
+        self.kernels = [name]
+        self.dominant = name
+        self.kernel_bytes = {name: self.bytes_per_step}
+        self.cfg["l2"] = (f"{nbuf} rotating input sets ({nbuf * self.bytes_per_step / 1e6:.0f} MB > 3x L2)"
+                          if nbuf > 1 else "inputs larger than L2; no flush")
+        self.config = self.cfg
+
+    def step(self, stream=None, events=None):
+        ops, b = self.ops, self.bufs[self.i % len(self.bufs)]
+        self.i += 1
+        if events is not None:
+            events[0].record(stream)
+        if self.name == "add_rms_norm":
+            ops.add_rms_norm(b[0], b[1], self.w, EPS, residual_out=b[2], normed_out=b[3], stream=stream)
+        elif self.name == "rms_norm_f32":
+            ops.rms_norm(b[0], self.w, EPS, out=b[1], stream=stream)
+        elif self.name == "rope":
+            ops.rope_embed(b[0], b[1], 0, THETA, self.table, stream=stream)
+        elif self.name == "swiglu":
+            ops.swiglu_ffn(b[0], b[1], out=b[2], stream=stream)
+        else:
+            ops.embedding_lookup(b[0], self.tab, SCALE, out=b[1], stream=stream)
+        if events is not None:
+            events[1].record(stream)
+        return 1
+
+    def e2e(self, steps):
+        """Per step: H2D of the inputs from pinned host memory, the kernel, D2H of the outputs."""
+        torch = self.torch
+        b = self.bufs[0]
+        n_in = {"add_rms_norm": 2, "rms_norm_f32": 1, "rope": 2, "swiglu": 2, "embedding": 1}[self.name]
+        outs = [0, 1] if self.name == "rope" else list(range(n_in, len(b)))
+        host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in b]
+        for h, t in zip(host, b):
+            h.copy_(t)
+        h2d = sum(host[i].numel() * host[i].element_size() for i in range(n_in))
+        d2h = sum(host[i].numel() * host[i].element_size() for i in outs)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches = 0
+        for it in range(steps + 1):  # iteration 0 is the warm-up
+            if it == 1:
+                torch.cuda.synchronize()
+                t0.record()
+            for i in range(n_in):
+                b[i].copy_(host[i], non_blocking=True)
+            self.i = 0
+            n = self.step()
+            launches += n if it else 0
+            for i in outs:
+                host[i].copy_(b[i], non_blocking=True)
+        t1.record()
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / steps, h2d, d2h, launches
+
+    def cpu_sample(self, min_seconds=5.0):
+        return None
+
+
+# ------------------------------------------------------------------ main
+def reference_arm(args, rank):
+    """The reference's path on the host cores: the oracle, all threads."""
+    if rank != 0:
+        return
+    if args.workload != "chain":
+        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the chain workload"}))
+        return
+    c = CpuChain()
+    for _ in range(args.warmup):
+        c.run_once()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        c.run_once()
+    sec = (time.perf_counter() - t0) / args.steps
+    gbs = c.bytes / sec / 1e9
+    from hrm_layer_ops.chain import algorithmic_bytes_per_token
+
+    tokens = CHAIN_S
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1000, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 math)",
+        "data": "synthetic (seeded numpy, host)",
+        "config": {"workload": "chain: embed+RMSNorm -> RoPE -> add+RMSNorm -> SwiGLU",
+                   "tokens_per_step": tokens, "hidden": HIDDEN, "intermediate": INTER,
+                   "bytes_per_token_minimal": algorithmic_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)["minimal"],
+                   "note": "each step is a bounded sample (4096 tokens) of the 65536-token pass"},
+        "rows_per_s": round(tokens / sec, 1),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": c.cores, "kind": "port",
+                         "sample": f"{c.tokens} tokens of the chain (one Q/K batch [1, 16, 4096, 128]) per step, "
+                                   f"oracle with {c.cores} OpenMP threads"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    wl = Chain(device, rank) if args.workload == "chain" else SingleOp(args.workload, device, rank)
+    stream = torch.cuda.current_stream(device)
+
+    for _ in range(args.warmup):
+        wl.step(stream)
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, per-kernel events on the launching stream
+    nk = len(wl.kernels)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            launches += wl.step(stream, evs[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_total = start.elapsed_time(end)
+    kern_ms = {k: sum(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps)) / args.steps
+               for j, k in enumerate(wl.kernels)}
+    if world > 1:
+        t = torch.tensor([ms_total] + [kern_ms[k] for k in wl.kernels], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t[0])
+        kern_ms = {k: float(t[j + 1]) for j, k in enumerate(wl.kernels)}
+    ms_step = ms_total / args.steps
+    value_gbs = world * wl.bytes_per_step / (ms_step / 1e3) / 1e9
+    rows_per_s = world * wl.rows_per_step / (ms_step / 1e3)
+
+    # ---- extras: decode latency, end-to-end, CPU baseline
+    decode_us = wl.decode_latency_us() if isinstance(wl, Chain) else None
+    e2e = None
+    if not args.no_e2e:
+        e2e_steps = max(2, min(args.steps, 5))
+        ms_e2e, h2d, d2h, _ = wl.e2e(e2e_steps)
+        if world > 1:
+            t = torch.tensor([ms_e2e], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_e2e = float(t[0])
+        e2e = {"value": round(world * wl.bytes_per_step / (ms_e2e / 1e3) / 1e9, 3), "unit": "GB/s",
+               "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "pinned host buffers, H2D / kernels / D2H overlapped in chunks (public API)"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu and isinstance(wl, Chain):
+        c = Chain.cpu_sample()
+        cpu = {"value": round(c["gbs"], 3), "unit": "GB/s", "cores": c["cores"], "kind": "port",
+               "sample": c["sample"]}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peak, peak_kind = load_peaks()
+    dom = wl.dominant
+    dom_ms = kern_ms[dom]
+    achieved = wl.kernel_bytes[dom] / (dom_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value_gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (fp32 math)", "data": "synthetic (seeded, generated on device)",
+        "config": dict(wl.config, parallelism=f"{world} row shards, no collective"),
+        "pct_of_peak": round(100 * value_gbs / (world * peak), 2), "rows_per_s": round(rows_per_s, 1),
+        "per_kernel": {k: {"us": round(kern_ms[k] * 1e3, 2),
+                           "gbs": round(wl.kernel_bytes[k] / (kern_ms[k] / 1e3) / 1e9, 1)} for k in wl.kernels},
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "bytes_per_launch": wl.kernel_bytes[dom],
+                     "traffic": load_traffic(dom, wl.name)},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    if decode_us is not None:
+        line["decode_64_tokens_us"] = round(decode_us, 2)
+    if e2e is not None:
+        line["e2e"] = e2e
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,58 @@
+// Shared device helpers for the sm_100a layer-op kernels.
+//
+// bf16 values travel as raw 16-bit patterns packed two per 32-bit word; a
+// 16-byte vector (uint4) carries 8 of them.  Conversions:
+//   bf16 -> f32 : exact, the pattern shifted into the high half of a binary32;
+//   f32  -> bf16: round-to-nearest-even via the cvt.rn.bf16x2.f32 instruction
+//                 (__float22bfloat162_rn), the rounding used by
+//                 __float2bfloat16 / __float22bfloat162_rn in the reference
+//                 kernels (e.g. src/kernels/additive_inject.cu:31).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hrm {
+
+// ---------------------------------------------------------------- bf16 <-> f32
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float bf16_to_f32(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+
+// Packs (lo, hi) into one word, each rounded to nearest even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 p = __float22bfloat162_rn(make_float2(lo, hi));
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+__device__ __forceinline__ uint16_t f32_to_bf16(float x) {
+  __nv_bfloat16 b = __float2bfloat16_rn(x);
+  return *reinterpret_cast<uint16_t*>(&b);
+}
+
+__device__ __forceinline__ uint32_t vget(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+__device__ __forceinline__ void vset(uint4& v, int i, uint32_t w) {
+  if (i == 0) v.x = w; else if (i == 1) v.y = w; else if (i == 2) v.z = w; else v.w = w;
+}
+
+// ------------------------------------------------------------- memory access
+// Streaming (read-once / write-once) accesses: evict-first in L1 and L2 so
+// that reused data (weights, rope tables, embedding rows) keeps its L2 lines.
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream(uint4* p, const uint4& v) { __stcs(p, v); }
+// Reused read-only data (weights, tables): normal caching.
+__device__ __forceinline__ uint4 ld_keep(const uint4* p) { return __ldg(p); }
+__device__ __forceinline__ float4 ld_keep(const float4* p) { return __ldg(p); }
+
+// ---------------------------------------------------------- async staging
+// cp.async (LDGSTS) of one 16-byte chunk global -> shared, L2-cached only.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+}  // namespace hrm

@@ -1,0 +1,115 @@
+// Elementwise bf16 streams: the SwiGLU gate and the residual add.
+//
+// Both are pure HBM streams (2 reads + 1 write per element, ~0.5 flop/B), so
+// the kernel is shaped for bytes in flight, not arithmetic:
+//   * one 16-byte vector (8 bf16) per access, every warp-wide access a fully
+//     used, contiguous 512-byte span;
+//   * U independent vectors per operand per thread issued before any use
+//     (U = 4 -> 8 x 16 B loads in flight per thread);
+//   * a grid of (SM count x resident CTAs) CTAs walking the tensor with a
+//     grid-sized stride, so no tail wave and no per-CTA index math;
+//   * evict-first loads/stores so the stream does not flush reused L2 lines.
+// The arithmetic per element is the reference's, operation for operation:
+//   swiglu: g * (1.0f / (1.0f + __expf(-g))) * u    (src/kernels/swiglu_ffn.cu:31-35)
+//   add   : a + b                                   (src/kernels/additive_inject.cu:29-31)
+// each rounded once to bf16 (RNE), so results match the reference bit for bit.
+#include "common.cuh"
+#include "launch.h"
+
+namespace hrm {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+struct SwigluOp {
+  __device__ __forceinline__ float f(float g, float u) const {
+    float sig = 1.0f / (1.0f + __expf(-g));
+    return g * sig * u;
+  }
+};
+struct AddOp {
+  __device__ __forceinline__ float f(float a, float b) const { return a + b; }
+};
+
+template <class Op>
+__device__ __forceinline__ uint4 apply8(const Op& op, const uint4& a, const uint4& b) {
+  uint4 o;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    uint32_t wa = vget(a, w), wb = vget(b, w);
+    vset(o, w, pack_bf16x2(op.f(bf16_lo(wa), bf16_lo(wb)), op.f(bf16_hi(wa), bf16_hi(wb))));
+  }
+  return o;
+}
+
+// a, b, out: 16-byte aligned; nvec = n / 8 full vectors; the n % 8 trailing
+// elements (starting at element nvec * 8) are done by global thread 0.
+template <class Op>
+__global__ void __launch_bounds__(kThreads) ew_vec_kernel(const uint4* a, const uint4* b, uint4* out,
+                                                          int64_t nvec, int tail) {
+  const Op op;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
+    uint4 va[kUnroll], vb[kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) {
+      va[j] = ld_stream(a + i + j * stride);
+      vb[j] = ld_stream(b + i + j * stride);
+    }
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) st_stream(out + i + j * stride, apply8(op, va[j], vb[j]));
+  }
+  for (; i < nvec; i += stride) st_stream(out + i, apply8(op, ld_stream(a + i), ld_stream(b + i)));
+
+  if (tail > 0 && blockIdx.x == 0 && threadIdx.x == 0) {
+    const uint16_t* as = reinterpret_cast<const uint16_t*>(a + nvec);
+    const uint16_t* bs = reinterpret_cast<const uint16_t*>(b + nvec);
+    uint16_t* os = reinterpret_cast<uint16_t*>(out + nvec);
+    for (int t = 0; t < tail; ++t) os[t] = f32_to_bf16(op.f(bf16_to_f32(as[t]), bf16_to_f32(bs[t])));
+  }
+}
+
+// Any alignment: one element per thread per step.
+template <class Op>
+__global__ void __launch_bounds__(kThreads) ew_scalar_kernel(const uint16_t* a, const uint16_t* b, uint16_t* out,
+                                                             int64_t n) {
+  const Op op;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride)
+    out[i] = f32_to_bf16(op.f(bf16_to_f32(a[i]), bf16_to_f32(b[i])));
+}
+
+template <class Op>
+cudaError_t launch_ew(const void* a, const void* b, void* out, int64_t n, cudaStream_t s) {
+  const int64_t max_blocks = (int64_t)device_sm_count() * (2048 / kThreads);
+  if (aligned16(a) && aligned16(b) && aligned16(out)) {
+    const int64_t nvec = n / 8;
+    int64_t blocks = (nvec + kThreads - 1) / kThreads;
+    if (blocks < 1) blocks = 1;
+    if (blocks > max_blocks) blocks = max_blocks;
+    ew_vec_kernel<Op><<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<const uint4*>(a),
+                                                            static_cast<const uint4*>(b),
+                                                            static_cast<uint4*>(out), nvec, (int)(n % 8));
+  } else {
+    int64_t blocks = (n + kThreads - 1) / kThreads;
+    if (blocks > max_blocks) blocks = max_blocks;
+    ew_scalar_kernel<Op><<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<const uint16_t*>(a),
+                                                               static_cast<const uint16_t*>(b),
+                                                               static_cast<uint16_t*>(out), n);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_swiglu(const void* gate, const void* up, void* out, int64_t n, cudaStream_t s) {
+  return launch_ew<SwigluOp>(gate, up, out, n, s);
+}
+
+cudaError_t launch_additive_inject(const void* a, const void* b, void* out, int64_t n, cudaStream_t s) {
+  return launch_ew<AddOp>(a, b, out, n, s);
+}
+
+}  // namespace hrm

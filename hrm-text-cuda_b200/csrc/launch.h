@@ -1,0 +1,35 @@
+// Host-side launchers of the sm_100a layer-op kernels (called by abi.cu after
+// argument validation; they assume valid, non-empty arguments).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hrm {
+
+// SM count of the current device, queried once per device and cached.
+int device_sm_count();
+
+// True when p is 16-byte aligned (a uint4 access is legal).
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaError_t launch_additive_inject(const void* a, const void* b, void* out, int64_t n, cudaStream_t s);
+cudaError_t launch_swiglu(const void* gate, const void* up, void* out, int64_t n, cudaStream_t s);
+
+cudaError_t launch_rms_norm_bf16(const void* x, void* y, const void* w, int64_t rows, int64_t hidden,
+                                 float eps, cudaStream_t s);
+cudaError_t launch_rms_norm_f32(const float* x, float* y, const float* w, int64_t rows, int64_t hidden,
+                                float eps, cudaStream_t s);
+cudaError_t launch_add_rms_norm(const void* x, const void* b, void* r, void* y, const void* w, int64_t rows,
+                                int64_t hidden, float eps, cudaStream_t s);
+cudaError_t launch_embed_rms_norm(const uint32_t* ids, const void* table, void* h, void* y, const void* w,
+                                  int64_t rows, int64_t hidden, int64_t vocab, float scale, float eps,
+                                  cudaStream_t s);
+cudaError_t launch_embedding(const uint32_t* ids, const void* table, void* out, int64_t tokens, int64_t hidden,
+                             int64_t vocab, float scale, cudaStream_t s);
+
+cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                        int64_t offset, float theta, const float* table, cudaStream_t s);
+cudaError_t launch_rope_table(float* table, int64_t max_pos, int64_t head_dim, float theta, cudaStream_t s);
+
+}  // namespace hrm

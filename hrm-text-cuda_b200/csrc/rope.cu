@@ -1,0 +1,225 @@
+// Rotary position embedding, in place on Q and K ([batch, heads, seq, head_dim]
+// bf16), rotate-half pairing (x[i], x[i + head_dim/2]) as in
+// src/kernels/rope_embed.cu:36-53.
+//
+// Fast path (head_dim % 16 == 0, head_dim <= 512, 16-byte aligned): a thread
+// owns 8 consecutive pairs of one row -- one 16-byte chunk of the low half and
+// the matching chunk of the high half -- so g = head_dim / 16 threads cover a
+// row (8 for head_dim 128).  A 128-thread CTA tile is pt positions x ht head
+// slices x g; each thread fetches the cos/sin of its 8 pairs at its position
+// once and reuses them for every head it visits (h = slice, slice + ht, ...)
+// and for both Q and K, so the angle work / table traffic is amortised over
+// 2 * heads rows.  Prefill tiles are 16 positions x 1 slice (each head's 16
+// rows are 4 KB contiguous); decode (seq 1) tiles are 1 position x 16 slices.
+// Four heads' worth of loads (16 x 16 B) are in flight before any store.
+//
+// Angles: either the fp32 table written by rope_table_kernel or, with no
+// table, evaluated in the thread with exactly the reference expression
+//   (float)(s + offset) * expf(-2.0f * i * logf(theta) / (float)head_dim)
+// and sincosf (src/kernels/rope_embed.cu:41-43).  The table is built with that
+// same expression, so both ways give the reference's cos/sin bit for bit, and
+// the rotation uses the reference's expression (x0*c - x1*s, x1*c + x0*s).
+#include "common.cuh"
+#include "launch.h"
+
+namespace hrm {
+namespace {
+
+constexpr int kThreads = 128;
+
+struct RopeArgs {
+  uint4* q;
+  uint4* k;
+  const float4* table;  // [positions][head_dim] floats: cos in [0, hd/2), sin in [hd/2, hd)
+  int64_t seq;
+  int64_t tiles_per_batch;
+  int64_t ntiles;
+  int heads;
+  int head_dim;
+  int g;   // threads per row (= chunks per half-row)
+  int pt;  // positions per tile
+  int ht;  // head slices per tile
+  int offset;
+  float theta;
+};
+
+__device__ __forceinline__ float rope_angle(int pos, int i, int head_dim, float theta) {
+  return (float)pos * expf(-2.0f * i * logf(theta) / (float)head_dim);
+}
+
+__device__ __forceinline__ void rotate8(uint4& lo, uint4& hi, const float (&c)[8], const float (&s)[8]) {
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t wl = vget(lo, w), wh = vget(hi, w);
+    const float x0a = bf16_lo(wl), x0b = bf16_hi(wl);
+    const float x1a = bf16_lo(wh), x1b = bf16_hi(wh);
+    const float ca = c[2 * w], sa = s[2 * w], cb = c[2 * w + 1], sb = s[2 * w + 1];
+    vset(lo, w, pack_bf16x2(x0a * ca - x1a * sa, x0b * cb - x1b * sb));
+    vset(hi, w, pack_bf16x2(x1a * ca + x0a * sa, x1b * cb + x0b * sb));
+  }
+}
+
+template <bool TABLE>
+__global__ void __launch_bounds__(kThreads) rope_tile_kernel(const RopeArgs a) {
+  const int j = threadIdx.x % a.g;
+  const int rest = threadIdx.x / a.g;
+  const int slice = rest % a.ht;
+  const int pl = rest / a.ht;
+  const int row_chunks = 2 * a.g;
+
+  for (int64_t tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
+    const int64_t b = tile / a.tiles_per_batch;
+    const int64_t s = (tile - b * a.tiles_per_batch) * a.pt + pl;
+    if (s >= a.seq) continue;
+    const int pos = (int)s + a.offset;
+
+    float c[8], sn[8];
+    if (TABLE) {
+      const float4* row = a.table + (int64_t)pos * (a.head_dim / 4);
+      const float4 c0 = ld_keep(row + 2 * j), c1 = ld_keep(row + 2 * j + 1);
+      const float4 s0 = ld_keep(row + a.head_dim / 8 + 2 * j), s1 = ld_keep(row + a.head_dim / 8 + 2 * j + 1);
+      c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sincosf(rope_angle(pos, 8 * j + e, a.head_dim, a.theta), &sn[e], &c[e]);
+    }
+
+    // Chunk index of (b, h, s) row start: ((b * heads + h) * seq + s) * row_chunks.
+    const int64_t head_step = a.seq * row_chunks;
+    const int64_t row0 = ((b * a.heads) * a.seq + s) * row_chunks + j;
+    int h = slice;
+    for (; h + 3 * a.ht < a.heads; h += 4 * a.ht) {
+      uint4 ql[4], qh[4], kl[4], kh[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t lo = row0 + (int64_t)(h + u * a.ht) * head_step;
+        ql[u] = ld_stream(a.q + lo);
+        qh[u] = ld_stream(a.q + lo + a.g);
+        kl[u] = ld_stream(a.k + lo);
+        kh[u] = ld_stream(a.k + lo + a.g);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t lo = row0 + (int64_t)(h + u * a.ht) * head_step;
+        rotate8(ql[u], qh[u], c, sn);
+        rotate8(kl[u], kh[u], c, sn);
+        st_stream(a.q + lo, ql[u]);
+        st_stream(a.q + lo + a.g, qh[u]);
+        st_stream(a.k + lo, kl[u]);
+        st_stream(a.k + lo + a.g, kh[u]);
+      }
+    }
+    for (; h < a.heads; h += a.ht) {
+      const int64_t lo = row0 + (int64_t)h * head_step;
+      uint4 ql = ld_stream(a.q + lo), qh = ld_stream(a.q + lo + a.g);
+      uint4 kl = ld_stream(a.k + lo), kh = ld_stream(a.k + lo + a.g);
+      rotate8(ql, qh, c, sn);
+      rotate8(kl, kh, c, sn);
+      st_stream(a.q + lo, ql);
+      st_stream(a.q + lo + a.g, qh);
+      st_stream(a.k + lo, kl);
+      st_stream(a.k + lo + a.g, kh);
+    }
+  }
+}
+
+// Any even head_dim / alignment: one thread per pair, as the reference maps
+// its threads (src/kernels/rope_embed.cu:22-37), with 64-bit indexing.
+__global__ void __launch_bounds__(256) rope_scalar_kernel(uint16_t* q, uint16_t* k, int64_t rows, int64_t seq,
+                                                          int head_dim, int offset, float theta,
+                                                          const float* table) {
+  const int half = head_dim / 2;
+  const int64_t total = rows * half;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+    const int i = (int)(idx % half);
+    const int64_t row = idx / half;
+    const int pos = (int)(row % seq) + offset;
+    float c, s;
+    if (table != nullptr) {
+      c = table[(int64_t)pos * head_dim + i];
+      s = table[(int64_t)pos * head_dim + half + i];
+    } else {
+      sincosf(rope_angle(pos, i, head_dim, theta), &s, &c);
+    }
+    const int64_t i0 = row * head_dim + i, i1 = i0 + half;
+    const float x0 = bf16_to_f32(q[i0]), x1 = bf16_to_f32(q[i1]);
+    q[i0] = f32_to_bf16(x0 * c - x1 * s);
+    q[i1] = f32_to_bf16(x1 * c + x0 * s);
+    const float k0 = bf16_to_f32(k[i0]), k1 = bf16_to_f32(k[i1]);
+    k[i0] = f32_to_bf16(k0 * c - k1 * s);
+    k[i1] = f32_to_bf16(k1 * c + k0 * s);
+  }
+}
+
+__global__ void __launch_bounds__(256) rope_table_kernel(float* table, int64_t positions, int head_dim,
+                                                         float theta) {
+  const int half = head_dim / 2;
+  const int64_t total = positions * half;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+    const int i = (int)(idx % half);
+    const int64_t p = idx / half;
+    float s, c;
+    sincosf(rope_angle((int)p, i, head_dim, theta), &s, &c);
+    table[p * head_dim + i] = c;
+    table[p * head_dim + half + i] = s;
+  }
+}
+
+int pow2_ceil(int64_t x) {
+  int p = 1;
+  while (p < x && p < (1 << 30)) p <<= 1;
+  return p;
+}
+
+}  // namespace
+
+cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                        int64_t offset, float theta, const float* table, cudaStream_t s) {
+  const int64_t sms = device_sm_count();
+  const int g = (int)(head_dim / 16);
+  const bool fast = head_dim % 16 == 0 && head_dim <= 512 && (g & (g - 1)) == 0 && aligned16(q) &&
+                    aligned16(k) && (table == nullptr || aligned16(table));
+  if (fast) {
+    RopeArgs a;
+    a.q = static_cast<uint4*>(q);
+    a.k = static_cast<uint4*>(k);
+    a.table = reinterpret_cast<const float4*>(table);
+    a.seq = seq;
+    a.heads = (int)heads;
+    a.head_dim = (int)head_dim;
+    a.g = g;
+    a.pt = pow2_ceil(seq);
+    if (a.pt > kThreads / g) a.pt = kThreads / g;
+    a.ht = kThreads / (g * a.pt);
+    a.tiles_per_batch = (seq + a.pt - 1) / a.pt;
+    a.ntiles = batch * a.tiles_per_batch;
+    a.offset = (int)offset;
+    a.theta = theta;
+    int64_t blocks = a.ntiles;
+    if (blocks > sms * 16) blocks = sms * 16;
+    if (table != nullptr)
+      rope_tile_kernel<true><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+    else
+      rope_tile_kernel<false><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+  } else {
+    const int64_t rows = batch * heads * seq;
+    int64_t blocks = (rows * (head_dim / 2) + 255) / 256;
+    if (blocks > sms * 8) blocks = sms * 8;
+    rope_scalar_kernel<<<(unsigned)blocks, 256, 0, s>>>(static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), rows,
+                                                        seq, (int)head_dim, (int)offset, theta, table);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_table(float* table, int64_t positions, int64_t head_dim, float theta, cudaStream_t s) {
+  int64_t blocks = (positions * (head_dim / 2) + 255) / 256;
+  const int64_t cap = (int64_t)device_sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  rope_table_kernel<<<(unsigned)blocks, 256, 0, s>>>(table, positions, (int)head_dim, theta);
+  return cudaGetLastError();
+}
+
+}  // namespace hrm

@@ -1,0 +1,522 @@
+// Row-normalising kernels: RMSNorm, residual-add + RMSNorm, embedding gather
+// + RMSNorm (bf16 I/O) and RMSNorm with fp32 I/O.
+//
+// Fast path (hidden % vector width == 0, hidden <= 4096 bf16 / 2048 fp32,
+// 16-byte aligned pointers): one warp per row, the whole row held in
+// registers, so the row is read from HBM exactly once (the reference reads it
+// twice, src/kernels/rms_norm.cu:28 and :62).  Lane l holds the 16-byte chunks
+// l, l+32, l+64, ... of its row, so every warp-wide access is one contiguous
+// 512-byte span.  A CTA of 8 warps stages the optional weight vector into
+// shared memory once with cp.async and then walks rows with a grid-sized
+// stride (the grid is one wave of resident CTAs).
+//
+// Reduction order.  rms_norm_kernel runs 256 threads per row: thread t
+// accumulates x[t], x[t+256], ... with fused multiply-add (src/kernels/
+// rms_norm.cu:28-31), then a shuffle-down tree in each warp (:34-37) and a
+// shuffle-down tree over the 8 warp sums (:44-55).  In the register layout a
+// lane's chunk j holds elements 8*lane + e + 256*j (bf16), i.e. exactly the
+// elements reference thread t = 8*lane + e accumulates, in the same order.
+// The lane keeps those 8 partial sums and replays the reference's two trees
+// with shuffles, so the sum of squares -- and with it every output -- is
+// bit-identical to the reference kernel's.  The fp32 variant follows the same
+// 256-thread order (4 elements per chunk; reference threads 4*lane + e and
+// 128 + 4*lane + e).
+//
+// Fallback (any hidden, any alignment): one 256-thread CTA per row with the
+// reference's own structure and two passes over the row.
+#include <atomic>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace hrm {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxVpl = 16;
+
+enum Mode { kRms = 0, kAdd = 1, kEmbed = 2 };
+
+struct RowArgs {
+  const uint4* x;        // kRms: input rows; kAdd: x rows; kEmbed: table rows
+  const uint4* b;        // kAdd: branch rows
+  const uint32_t* ids;   // kEmbed: token ids, one per row
+  uint4* r;              // kAdd: residual out; kEmbed: gathered rows out (may be null)
+  uint4* y;              // normed out
+  const uint4* w;        // weight (null: parameterless)
+  int64_t rows;
+  int nchunks;           // 16-byte chunks per row
+  int hidden;            // elements per row
+  uint32_t vocab;        // kEmbed
+  float scale;           // kEmbed
+  float eps;
+};
+
+// ---------------------------------------------------------------- reductions
+// bf16 layout: p[e] is the partial sum of reference thread 8*lane + e.
+// Reference warp w covers threads 32w..32w+31 = lanes 4w..4w+3, element
+// slot m = 8*(lane%4) + e.  Returns the row total in every lane.
+__device__ __forceinline__ float ref_tree_bf16(float (&p)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) p[e] += __shfl_down_sync(0xffffffffu, p[e], 2);  // m + 16
+#pragma unroll
+  for (int e = 0; e < 8; ++e) p[e] += __shfl_down_sync(0xffffffffu, p[e], 1);  // m + 8
+  const float q0 = p[0] + p[4], q1 = p[1] + p[5], q2 = p[2] + p[6], q3 = p[3] + p[7];  // m + 4
+  const float r0 = q0 + q2, r1 = q1 + q3;                                               // m + 2
+  float s = r0 + r1;                                                                    // m + 1
+  // lane 4w now holds warp w's sum; tree over the 8 warps (offsets 4, 2, 1).
+  s += __shfl_down_sync(0xffffffffu, s, 16);
+  s += __shfl_down_sync(0xffffffffu, s, 8);
+  s += __shfl_down_sync(0xffffffffu, s, 4);
+  return __shfl_sync(0xffffffffu, s, 0);
+}
+
+// fp32 layout: a[e] = reference thread 4*lane + e (chunks j even),
+// c[e] = reference thread 128 + 4*lane + e (chunks j odd).  Reference warp
+// w < 4 covers lanes 8w..8w+7 of a, warp w + 4 the same lanes of c, element
+// slot m = 4*(lane%8) + e.
+__device__ __forceinline__ float ref_tree_f32(float (&a)[4], float (&c)[4]) {
+#pragma unroll
+  for (int off = 4; off >= 1; off >>= 1) {  // m + 16, m + 8, m + 4
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      a[e] += __shfl_down_sync(0xffffffffu, a[e], off);
+      c[e] += __shfl_down_sync(0xffffffffu, c[e], off);
+    }
+  }
+  const float ra = (a[0] + a[2]) + (a[1] + a[3]);  // m + 2, m + 1
+  const float rc = (c[0] + c[2]) + (c[1] + c[3]);
+  float s = ra + rc;                               // warp w + warp w+4
+  s += __shfl_down_sync(0xffffffffu, s, 16);       // + warp w+2
+  s += __shfl_down_sync(0xffffffffu, s, 8);        // + warp w+1
+  return __shfl_sync(0xffffffffu, s, 0);
+}
+
+// inv = 1 / sqrtf(ss / hidden + eps), as src/kernels/rms_norm.cu:58-59.
+__device__ __forceinline__ float inv_rms(float ss, int hidden, float eps) {
+  const float rms = sqrtf(ss / (float)hidden + eps);
+  return 1.0f / rms;
+}
+
+__device__ __forceinline__ uint4 add8(const uint4& a, const uint4& b) {
+  uint4 o;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t wa = vget(a, w), wb = vget(b, w);
+    vset(o, w, pack_bf16x2(bf16_lo(wa) + bf16_lo(wb), bf16_hi(wa) + bf16_hi(wb)));
+  }
+  return o;
+}
+
+__device__ __forceinline__ uint4 scale8(const uint4& a, float scale) {
+  uint4 o;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t wa = vget(a, w);
+    vset(o, w, pack_bf16x2(bf16_lo(wa) * scale, bf16_hi(wa) * scale));
+  }
+  return o;
+}
+
+template <bool HAS_W>
+__device__ __forceinline__ uint4 norm8(const uint4& v, float inv, const uint4& wv) {
+  uint4 o;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t wa = vget(v, w);
+    float lo = bf16_lo(wa) * inv, hi = bf16_hi(wa) * inv;
+    if (HAS_W) {
+      const uint32_t ww = vget(wv, w);
+      lo = lo * bf16_lo(ww);
+      hi = hi * bf16_hi(ww);
+    }
+    vset(o, w, pack_bf16x2(lo, hi));
+  }
+  return o;
+}
+
+__device__ __forceinline__ void accum8(float (&p)[8], const uint4& v) {
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t wa = vget(v, w);
+    const float lo = bf16_lo(wa), hi = bf16_hi(wa);
+    p[2 * w] = fmaf(lo, lo, p[2 * w]);
+    p[2 * w + 1] = fmaf(hi, hi, p[2 * w + 1]);
+  }
+}
+
+// Stages `nchunks` 16-byte chunks of w into shared memory (whole CTA).
+__device__ __forceinline__ void stage_weight(uint4* s_w, const uint4* w, int nchunks) {
+  for (int c = threadIdx.x; c < nchunks; c += kThreads) cp_async16(&s_w[c], w + c);
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+}
+
+// ------------------------------------------------------------ bf16 fast path
+template <int VPL, int MODE, bool HAS_W>
+__global__ void __launch_bounds__(kThreads) rownorm_warp_kernel(const RowArgs a) {
+  extern __shared__ uint4 s_w[];
+  const int lane = threadIdx.x & 31;
+  if (HAS_W) stage_weight(s_w, a.w, a.nchunks);
+
+  const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < a.rows; row += warp_stride) {
+    const uint4* src;
+    if (MODE == kEmbed) {
+      uint32_t id = a.ids[row];
+      if (id >= a.vocab) id = a.vocab - 1;  // src/kernels/embedding_lookup.cu:35
+      src = a.x + (int64_t)id * a.nchunks;
+    } else {
+      src = a.x + row * a.nchunks;
+    }
+    const int64_t base = row * a.nchunks;
+
+    uint4 v[VPL];
+    uint4 vb[MODE == kAdd ? VPL : 1];
+    // All loads first (r may alias x / b, so no store may precede a load).
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) {
+        if (MODE == kEmbed) {
+          v[j] = ld_keep(src + c);  // table rows may repeat: keep them in L2
+        } else {
+          v[j] = ld_stream(src + c);
+          if (MODE == kAdd) vb[j] = ld_stream(a.b + base + c);
+        }
+      }
+    }
+    float p[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) p[e] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) {
+        if (MODE == kAdd) {
+          v[j] = add8(v[j], vb[j]);
+          st_stream(a.r + base + c, v[j]);
+        } else if (MODE == kEmbed) {
+          v[j] = scale8(v[j], a.scale);
+          if (a.r != nullptr) st_stream(a.r + base + c, v[j]);
+        }
+        accum8(p, v[j]);
+      }
+    }
+    const float inv = inv_rms(ref_tree_bf16(p), a.hidden, a.eps);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) {
+        uint4 wv = make_uint4(0, 0, 0, 0);
+        if (HAS_W) wv = s_w[c];
+        st_stream(a.y + base + c, norm8<HAS_W>(v[j], inv, wv));
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------ fp32 fast path
+struct RowArgsF32 {
+  const float4* x;
+  float4* y;
+  const float4* w;
+  int64_t rows;
+  int nchunks;  // hidden / 4
+  int hidden;
+  float eps;
+};
+
+template <int VPL, bool HAS_W>
+__global__ void __launch_bounds__(kThreads) rms_f32_warp_kernel(const RowArgsF32 a) {
+  extern __shared__ uint4 s_w4[];
+  float4* s_w = reinterpret_cast<float4*>(s_w4);
+  const int lane = threadIdx.x & 31;
+  if (HAS_W) stage_weight(s_w4, reinterpret_cast<const uint4*>(a.w), a.nchunks);
+
+  const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < a.rows; row += warp_stride) {
+    const int64_t base = row * a.nchunks;
+    float4 v[VPL];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) v[j] = __ldcs(a.x + base + c);
+    }
+    float pa[4] = {0.f, 0.f, 0.f, 0.f}, pc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) {
+        float(&p)[4] = (j & 1) ? pc : pa;
+        p[0] = fmaf(v[j].x, v[j].x, p[0]);
+        p[1] = fmaf(v[j].y, v[j].y, p[1]);
+        p[2] = fmaf(v[j].z, v[j].z, p[2]);
+        p[3] = fmaf(v[j].w, v[j].w, p[3]);
+      }
+    }
+    const float inv = inv_rms(ref_tree_f32(pa, pc), a.hidden, a.eps);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) {
+        float4 o = make_float4(v[j].x * inv, v[j].y * inv, v[j].z * inv, v[j].w * inv);
+        if (HAS_W) {
+          const float4 wv = s_w[c];
+          o.x = o.x * wv.x; o.y = o.y * wv.y; o.z = o.z * wv.z; o.w = o.w * wv.w;
+        }
+        __stcs(a.y + base + c, o);
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------- fallback (any shape)
+// One CTA of 256 threads per row, the reference's structure: strided
+// accumulation, shuffle-down tree per warp, tree over the warp sums, then a
+// second pass that produces the outputs.
+struct RowArgsScalar {
+  const void* x;         // T rows (kRms / kAdd) or bf16 table (kEmbed)
+  const uint16_t* b;     // kAdd
+  const uint32_t* ids;   // kEmbed
+  uint16_t* r;           // kAdd residual / kEmbed hidden (nullable)
+  void* y;               // T rows
+  const void* w;         // T [hidden] or null
+  int64_t rows;
+  int64_t hidden;
+  uint32_t vocab;
+  float scale, eps;
+};
+
+template <typename T> __device__ __forceinline__ float load_t(const void* p, int64_t i);
+template <> __device__ __forceinline__ float load_t<uint16_t>(const void* p, int64_t i) {
+  return bf16_to_f32(static_cast<const uint16_t*>(p)[i]);
+}
+template <> __device__ __forceinline__ float load_t<float>(const void* p, int64_t i) {
+  return static_cast<const float*>(p)[i];
+}
+template <typename T> __device__ __forceinline__ void store_t(void* p, int64_t i, float v);
+template <> __device__ __forceinline__ void store_t<uint16_t>(void* p, int64_t i, float v) {
+  static_cast<uint16_t*>(p)[i] = f32_to_bf16(v);
+}
+template <> __device__ __forceinline__ void store_t<float>(void* p, int64_t i, float v) {
+  static_cast<float*>(p)[i] = v;
+}
+
+template <typename T, int MODE, bool HAS_W>
+__global__ void __launch_bounds__(kThreads) rownorm_block_kernel(const RowArgsScalar a) {
+  __shared__ float s_sums[kWarps];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.hidden;
+    int64_t src = base;
+    if (MODE == kEmbed) {
+      uint32_t id = a.ids[row];
+      if (id >= a.vocab) id = a.vocab - 1;
+      src = (int64_t)id * a.hidden;
+    }
+    float local = 0.0f;
+    for (int64_t i = tid; i < a.hidden; i += kThreads) {
+      float v;
+      if (MODE == kAdd) {
+        v = bf16_to_f32(f32_to_bf16(load_t<uint16_t>(a.x, base + i) + bf16_to_f32(a.b[base + i])));
+        a.r[base + i] = f32_to_bf16(v);
+      } else if (MODE == kEmbed) {
+        v = bf16_to_f32(f32_to_bf16(load_t<uint16_t>(a.x, src + i) * a.scale));
+        if (a.r != nullptr) a.r[base + i] = f32_to_bf16(v);
+      } else {
+        v = load_t<T>(a.x, base + i);
+      }
+      local = fmaf(v, v, local);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) local += __shfl_down_sync(0xffffffffu, local, off);
+    if (lane == 0) s_sums[warp] = local;
+    __syncthreads();
+    if (warp == 0) {
+      // Lane 0's result is the reference's tree over the 8 warp sums
+      // (offsets 4, 2, 1); lanes >= 8 only feed lanes that are not used.
+      float val = lane < kWarps ? s_sums[lane] : 0.0f;
+#pragma unroll
+      for (int off = kWarps / 2; off > 0; off >>= 1) val += __shfl_down_sync(0xffffffffu, val, off);
+      if (lane == 0) s_sums[0] = val;
+    }
+    __syncthreads();
+    const float inv = inv_rms(s_sums[0], (int)a.hidden, a.eps);
+    __syncthreads();  // s_sums is rewritten by the next row
+    for (int64_t i = tid; i < a.hidden; i += kThreads) {
+      float v;
+      if (MODE == kAdd) {
+        v = bf16_to_f32(a.r[base + i]);  // written above by this same thread
+      } else if (MODE == kEmbed) {
+        v = bf16_to_f32(f32_to_bf16(load_t<uint16_t>(a.x, src + i) * a.scale));
+      } else {
+        v = load_t<T>(a.x, base + i);
+      }
+      float o = v * inv;
+      if (HAS_W) o = o * load_t<T>(a.w, i);
+      store_t<T>(a.y, base + i, o);
+    }
+  }
+}
+
+// ------------------------------------------------------------ dispatch
+template <typename K>
+int resident_ctas(K kernel, size_t smem) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem) != cudaSuccess || n < 1) n = 1;
+  return n;
+}
+
+template <int VPL, int MODE, bool HAS_W>
+cudaError_t launch_warp_on(const RowArgs& a, cudaStream_t s) {
+  auto kernel = rownorm_warp_kernel<VPL, MODE, HAS_W>;
+  static std::atomic<int> occ{0};  // resident CTAs per SM (smem <= 8 KB never limits it)
+  int o = occ.load(std::memory_order_relaxed);
+  if (o == 0) {
+    o = resident_ctas(kernel, (size_t)kMaxVpl * 32 * 16);
+    occ.store(o, std::memory_order_relaxed);
+  }
+  const size_t smem = HAS_W ? (size_t)a.nchunks * 16 : 0;
+  int64_t blocks = (a.rows + kWarps - 1) / kWarps;
+  const int64_t wave = (int64_t)device_sm_count() * o;
+  if (blocks > wave) blocks = wave;
+  kernel<<<(unsigned)blocks, kThreads, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <int MODE, bool HAS_W>
+cudaError_t dispatch_vpl(const RowArgs& a, cudaStream_t s) {
+  const int need = (a.nchunks + 31) / 32;
+  if (need <= 1) return launch_warp_on<1, MODE, HAS_W>(a, s);
+  if (need <= 2) return launch_warp_on<2, MODE, HAS_W>(a, s);
+  if (need <= 4) return launch_warp_on<4, MODE, HAS_W>(a, s);
+  if (need <= 6) return launch_warp_on<6, MODE, HAS_W>(a, s);
+  if (need <= 8) return launch_warp_on<8, MODE, HAS_W>(a, s);
+  return launch_warp_on<16, MODE, HAS_W>(a, s);
+}
+
+template <typename T, int MODE, bool HAS_W>
+cudaError_t launch_block(const RowArgsScalar& a, cudaStream_t s) {
+  int64_t blocks = a.rows;
+  const int64_t cap = (int64_t)device_sm_count() * 64;
+  if (blocks > cap) blocks = cap;
+  rownorm_block_kernel<T, MODE, HAS_W><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_bf16_rows(const void* x, const void* b, const uint32_t* ids, void* r, void* y, const void* w,
+                             int64_t rows, int64_t hidden, int64_t vocab, float scale, float eps, cudaStream_t s) {
+  const bool fast = hidden % 8 == 0 && hidden / 8 <= kMaxVpl * 32 && aligned16(x) && aligned16(y) &&
+                    (b == nullptr || aligned16(b)) && (r == nullptr || aligned16(r)) &&
+                    (w == nullptr || aligned16(w));
+  if (fast) {
+    RowArgs a;
+    a.x = static_cast<const uint4*>(x);
+    a.b = static_cast<const uint4*>(b);
+    a.ids = ids;
+    a.r = static_cast<uint4*>(r);
+    a.y = static_cast<uint4*>(y);
+    a.w = static_cast<const uint4*>(w);
+    a.rows = rows;
+    a.nchunks = (int)(hidden / 8);
+    a.hidden = (int)hidden;
+    a.vocab = (uint32_t)vocab;
+    a.scale = scale;
+    a.eps = eps;
+    return w ? dispatch_vpl<MODE, true>(a, s) : dispatch_vpl<MODE, false>(a, s);
+  }
+  RowArgsScalar a;
+  a.x = x;
+  a.b = static_cast<const uint16_t*>(b);
+  a.ids = ids;
+  a.r = static_cast<uint16_t*>(r);
+  a.y = y;
+  a.w = w;
+  a.rows = rows;
+  a.hidden = hidden;
+  a.vocab = (uint32_t)vocab;
+  a.scale = scale;
+  a.eps = eps;
+  return w ? launch_block<uint16_t, MODE, true>(a, s) : launch_block<uint16_t, MODE, false>(a, s);
+}
+
+template <int VPL, bool HAS_W>
+cudaError_t launch_f32_warp(const RowArgsF32& a, cudaStream_t s) {
+  auto kernel = rms_f32_warp_kernel<VPL, HAS_W>;
+  static std::atomic<int> occ{0};
+  int o = occ.load(std::memory_order_relaxed);
+  if (o == 0) {
+    o = resident_ctas(kernel, (size_t)kMaxVpl * 32 * 16);
+    occ.store(o, std::memory_order_relaxed);
+  }
+  const size_t smem = HAS_W ? (size_t)a.nchunks * 16 : 0;
+  int64_t blocks = (a.rows + kWarps - 1) / kWarps;
+  const int64_t wave = (int64_t)device_sm_count() * o;
+  if (blocks > wave) blocks = wave;
+  kernel<<<(unsigned)blocks, kThreads, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <bool HAS_W>
+cudaError_t dispatch_f32(const RowArgsF32& a, cudaStream_t s) {
+  const int need = (a.nchunks + 31) / 32;
+  if (need <= 1) return launch_f32_warp<1, HAS_W>(a, s);
+  if (need <= 2) return launch_f32_warp<2, HAS_W>(a, s);
+  if (need <= 4) return launch_f32_warp<4, HAS_W>(a, s);
+  if (need <= 8) return launch_f32_warp<8, HAS_W>(a, s);
+  return launch_f32_warp<16, HAS_W>(a, s);
+}
+
+}  // namespace
+
+cudaError_t launch_rms_norm_bf16(const void* x, void* y, const void* w, int64_t rows, int64_t hidden, float eps,
+                                 cudaStream_t s) {
+  return launch_bf16_rows<kRms>(x, nullptr, nullptr, nullptr, y, w, rows, hidden, 0, 1.0f, eps, s);
+}
+
+cudaError_t launch_add_rms_norm(const void* x, const void* b, void* r, void* y, const void* w, int64_t rows,
+                                int64_t hidden, float eps, cudaStream_t s) {
+  return launch_bf16_rows<kAdd>(x, b, nullptr, r, y, w, rows, hidden, 0, 1.0f, eps, s);
+}
+
+cudaError_t launch_embed_rms_norm(const uint32_t* ids, const void* table, void* h, void* y, const void* w,
+                                  int64_t rows, int64_t hidden, int64_t vocab, float scale, float eps,
+                                  cudaStream_t s) {
+  return launch_bf16_rows<kEmbed>(table, nullptr, ids, h, y, w, rows, hidden, vocab, scale, eps, s);
+}
+
+cudaError_t launch_rms_norm_f32(const float* x, float* y, const float* w, int64_t rows, int64_t hidden, float eps,
+                                cudaStream_t s) {
+  const bool fast = hidden % 4 == 0 && hidden / 4 <= kMaxVpl * 32 && aligned16(x) && aligned16(y) &&
+                    (w == nullptr || aligned16(w));
+  if (fast) {
+    RowArgsF32 a;
+    a.x = reinterpret_cast<const float4*>(x);
+    a.y = reinterpret_cast<float4*>(y);
+    a.w = reinterpret_cast<const float4*>(w);
+    a.rows = rows;
+    a.nchunks = (int)(hidden / 4);
+    a.hidden = (int)hidden;
+    a.eps = eps;
+    return w ? dispatch_f32<true>(a, s) : dispatch_f32<false>(a, s);
+  }
+  RowArgsScalar a;
+  a.x = x;
+  a.b = nullptr;
+  a.ids = nullptr;
+  a.r = nullptr;
+  a.y = y;
+  a.w = w;
+  a.rows = rows;
+  a.hidden = hidden;
+  a.vocab = 0;
+  a.scale = 1.0f;
+  a.eps = eps;
+  return w ? launch_block<float, kRms, true>(a, s) : launch_block<float, kRms, false>(a, s);
+}
+
+}  // namespace hrm

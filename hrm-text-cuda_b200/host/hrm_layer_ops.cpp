@@ -1,0 +1,198 @@
+// Implementation of the C++ host layer (see hrm_layer_ops.hpp).
+#include "hrm_layer_ops.hpp"
+
+#include <cstring>
+#include <string>
+
+namespace hrm {
+
+namespace {
+
+[[noreturn]] void fail(HrmError::Kind kind, int status, const std::string& what) { throw HrmError(kind, status, what); }
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess)
+    fail(HrmError::Kind::Driver, HRM_ERR_CUDA + (int)e, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <class T>
+void need(const CudaSlice<T>& s, size_t elems, const char* op, const char* name) {
+  if (s.len() < elems)
+    fail(HrmError::Kind::InvalidInput, HRM_ERR_INVALID_SHAPE,
+         std::string(op) + ": " + name + " holds " + std::to_string(s.len()) + " elements, " +
+             std::to_string(elems) + " required");
+}
+
+}  // namespace
+
+bf16 bf16::from_f32(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  bf16 r;
+  if ((u & 0x7fffffffu) > 0x7f800000u) {
+    r.bits = 0x7fffu;
+  } else {
+    u += 0x7fffu + ((u >> 16) & 1u);
+    r.bits = (uint16_t)(u >> 16);
+  }
+  return r;
+}
+
+float bf16::to_f32() const {
+  const uint32_t u = (uint32_t)bits << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+HrmLayerOps::HrmLayerOps(int dev_ordinal, HrmConfig cfg) : config(cfg), dev_(dev_ordinal) {
+  if (hrm_abi_version() / 10000 != 1)
+    fail(HrmError::Kind::KernelNotFound, 0, "libhrm_ops ABI major version mismatch");
+  cuda_check(cudaSetDevice(dev_ordinal), "cudaSetDevice");
+  cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+}
+
+HrmLayerOps::~HrmLayerOps() {
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+void HrmLayerOps::check(int status, const char* op) const {
+  if (status == HRM_OK) return;
+  const HrmError::Kind kind = status >= HRM_ERR_CUDA ? HrmError::Kind::Driver : HrmError::Kind::InvalidInput;
+  fail(kind, status, std::string(op) + ": " + hrm_status_string(status));
+}
+
+CudaSlice<bf16> HrmLayerOps::alloc_zero_bf16(size_t len) const {
+  void* p = nullptr;
+  cuda_check(cudaMalloc(&p, len * sizeof(bf16) + (len == 0)), "cudaMalloc");
+  CudaSlice<bf16> s(static_cast<bf16*>(p), len);
+  cuda_check(cudaMemsetAsync(p, 0, len * sizeof(bf16), stream_), "cudaMemsetAsync");
+  return s;
+}
+
+CudaSlice<bf16> HrmLayerOps::htod_copy_bf16(const std::vector<bf16>& host) const {
+  CudaSlice<bf16> s = alloc_zero_bf16(host.size());
+  cuda_check(cudaMemcpyAsync(s.device_ptr(), host.data(), host.size() * sizeof(bf16), cudaMemcpyHostToDevice, stream_),
+             "cudaMemcpyAsync");
+  cuda_check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");  // host vector may die after return
+  return s;
+}
+
+CudaSlice<uint32_t> HrmLayerOps::htod_copy_u32(const std::vector<uint32_t>& host) const {
+  void* p = nullptr;
+  cuda_check(cudaMalloc(&p, host.size() * sizeof(uint32_t) + host.empty()), "cudaMalloc");
+  CudaSlice<uint32_t> s(static_cast<uint32_t*>(p), host.size());
+  cuda_check(cudaMemcpyAsync(p, host.data(), host.size() * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_),
+             "cudaMemcpyAsync");
+  cuda_check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  return s;
+}
+
+std::vector<bf16> HrmLayerOps::sync_reclaim(CudaSlice<bf16>&& slice) const {
+  std::vector<bf16> host(slice.len());
+  cuda_check(cudaMemcpyAsync(host.data(), slice.device_ptr(), slice.len() * sizeof(bf16), cudaMemcpyDeviceToHost,
+                             stream_),
+             "cudaMemcpyAsync");
+  cuda_check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  CudaSlice<bf16> drop(std::move(slice));
+  return host;
+}
+
+void HrmLayerOps::additive_inject(const CudaSlice<bf16>& z_a, const CudaSlice<bf16>& z_b, CudaSlice<bf16>& z_out,
+                                  size_t total_elements) const {
+  need(z_a, total_elements, "additive_inject", "z_a");
+  need(z_b, total_elements, "additive_inject", "z_b");
+  need(z_out, total_elements, "additive_inject", "z_out");
+  check(hrm_additive_inject(z_a.device_ptr(), z_b.device_ptr(), z_out.device_ptr(), (int64_t)total_elements,
+                            stream_),
+        "additive_inject");
+}
+
+void HrmLayerOps::rms_norm(const CudaSlice<bf16>& input, CudaSlice<bf16>& output, size_t rows,
+                           size_t hidden_size) const {
+  need(input, rows * hidden_size, "rms_norm", "input");
+  need(output, rows * hidden_size, "rms_norm", "output");
+  check(hrm_rms_norm(input.device_ptr(), output.device_ptr(), nullptr, (int64_t)rows, (int64_t)hidden_size,
+                     config.norm_eps, stream_),
+        "rms_norm");
+}
+
+void HrmLayerOps::rope_embed(CudaSlice<bf16>& q, CudaSlice<bf16>& k, size_t batch_size, size_t num_heads,
+                             size_t seq_len, size_t head_dim, size_t position_offset) const {
+  const size_t n = batch_size * num_heads * seq_len * head_dim;
+  need(q, n, "rope_embed", "q");
+  need(k, n, "rope_embed", "k");
+  const bool use_table = rope_table_.device_ptr() != nullptr && head_dim == config.head_dim &&
+                         position_offset + seq_len <= rope_positions_;
+  check(hrm_rope_embed(q.device_ptr(), k.device_ptr(), (int64_t)batch_size, (int64_t)num_heads, (int64_t)seq_len,
+                       (int64_t)head_dim, (int64_t)position_offset, config.rope_theta,
+                       use_table ? rope_table_.device_ptr() : nullptr, use_table ? (int64_t)rope_positions_ : 0,
+                       stream_),
+        "rope_embed");
+}
+
+void HrmLayerOps::swiglu_ffn(const CudaSlice<bf16>& gate, const CudaSlice<bf16>& up, CudaSlice<bf16>& output,
+                             size_t total_elements) const {
+  need(gate, total_elements, "swiglu_ffn", "gate");
+  need(up, total_elements, "swiglu_ffn", "up");
+  need(output, total_elements, "swiglu_ffn", "output");
+  check(hrm_swiglu_ffn(gate.device_ptr(), up.device_ptr(), output.device_ptr(), (int64_t)total_elements, stream_),
+        "swiglu_ffn");
+}
+
+void HrmLayerOps::embedding_lookup(const CudaSlice<uint32_t>& input_ids, const CudaSlice<bf16>& embedding_table,
+                                   CudaSlice<bf16>& output, size_t batch_size, size_t seq_len, size_t hidden_size,
+                                   size_t vocab_size, float embedding_scale) const {
+  need(input_ids, batch_size * seq_len, "embedding_lookup", "input_ids");
+  need(embedding_table, vocab_size * hidden_size, "embedding_lookup", "embedding_table");
+  need(output, batch_size * seq_len * hidden_size, "embedding_lookup", "output");
+  check(hrm_embedding_lookup(input_ids.device_ptr(), embedding_table.device_ptr(), output.device_ptr(),
+                             (int64_t)batch_size, (int64_t)seq_len, (int64_t)hidden_size, (int64_t)vocab_size,
+                             embedding_scale, stream_),
+        "embedding_lookup");
+}
+
+void HrmLayerOps::add_rms_norm(const CudaSlice<bf16>& x, const CudaSlice<bf16>& branch, CudaSlice<bf16>& residual_out,
+                               CudaSlice<bf16>& normed_out, const CudaSlice<bf16>* weight, size_t rows,
+                               size_t hidden_size) const {
+  const size_t n = rows * hidden_size;
+  need(x, n, "add_rms_norm", "x");
+  need(branch, n, "add_rms_norm", "branch");
+  need(residual_out, n, "add_rms_norm", "residual_out");
+  need(normed_out, n, "add_rms_norm", "normed_out");
+  if (weight) need(*weight, hidden_size, "add_rms_norm", "weight");
+  check(hrm_add_rms_norm(x.device_ptr(), branch.device_ptr(), residual_out.device_ptr(), normed_out.device_ptr(),
+                         weight ? weight->device_ptr() : nullptr, (int64_t)rows, (int64_t)hidden_size,
+                         config.norm_eps, stream_),
+        "add_rms_norm");
+}
+
+void HrmLayerOps::embed_rms_norm(const CudaSlice<uint32_t>& input_ids, const CudaSlice<bf16>& embedding_table,
+                                 CudaSlice<bf16>* hidden_out, CudaSlice<bf16>& normed_out,
+                                 const CudaSlice<bf16>* weight, size_t rows, size_t hidden_size, size_t vocab_size,
+                                 float embedding_scale) const {
+  need(input_ids, rows, "embed_rms_norm", "input_ids");
+  need(embedding_table, vocab_size * hidden_size, "embed_rms_norm", "embedding_table");
+  need(normed_out, rows * hidden_size, "embed_rms_norm", "normed_out");
+  if (hidden_out) need(*hidden_out, rows * hidden_size, "embed_rms_norm", "hidden_out");
+  if (weight) need(*weight, hidden_size, "embed_rms_norm", "weight");
+  check(hrm_embed_rms_norm(input_ids.device_ptr(), embedding_table.device_ptr(),
+                           hidden_out ? hidden_out->device_ptr() : nullptr, normed_out.device_ptr(),
+                           weight ? weight->device_ptr() : nullptr, (int64_t)rows, (int64_t)hidden_size,
+                           (int64_t)vocab_size, embedding_scale, config.norm_eps, stream_),
+        "embed_rms_norm");
+}
+
+void HrmLayerOps::build_rope_table(size_t max_positions) {
+  void* p = nullptr;
+  const size_t n = max_positions * config.head_dim;
+  cuda_check(cudaMalloc(&p, n * sizeof(float) + (n == 0)), "cudaMalloc");
+  CudaSlice<float> table(static_cast<float*>(p), n);
+  check(hrm_rope_table_build(table.device_ptr(), (int64_t)max_positions, (int64_t)config.head_dim,
+                             config.rope_theta, stream_),
+        "rope_table_build");
+  rope_table_ = std::move(table);
+  rope_positions_ = max_positions;
+}
+
+}  // namespace hrm

@@ -1,0 +1,138 @@
+// C++ host layer over the C ABI (include/hrm_ops.h), mirroring the kernel
+// wrapper methods of the reference's `HrmForwardPass` (src/lib.rs:154-565):
+// same method names, argument order and meaning, hyper-parameters read from
+// an HrmConfig, and failures reported as an HrmError of the same kinds as the
+// reference's error enum (src/lib.rs:5-19).  Rust's `CudaResult<()>` maps to
+// a void method that throws HrmError.
+//
+// Device memory follows cudarc's CudaSlice<T> (an owned, typed allocation on
+// one device); the layer owns one CUDA stream, the analogue of
+// `CudaDevice::cu_stream()`, and every launch is queued on it.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "hrm_ops.h"
+
+namespace hrm {
+
+// IEEE bfloat16 storage, as half::bf16 (round-to-nearest-even from f32).
+struct bf16 {
+  uint16_t bits = 0;
+  static bf16 from_f32(float f);
+  float to_f32() const;
+};
+
+// Mirrors HrmError (src/lib.rs:5-19): Driver = a CUDA error, InvalidInput =
+// a rejected argument, KernelNotFound = the kernel library is not usable.
+class HrmError : public std::runtime_error {
+ public:
+  enum class Kind { Driver, InvalidInput, KernelNotFound };
+  HrmError(Kind kind, int status, const std::string& what)
+      : std::runtime_error(what), kind_(kind), status_(status) {}
+  Kind kind() const { return kind_; }
+  int status() const { return status_; }
+
+ private:
+  Kind kind_;
+  int status_;
+};
+
+// Mirrors HrmConfig and its defaults (src/lib.rs:24-60).
+struct HrmConfig {
+  size_t hidden_size = 1536;
+  size_t num_heads = 12;
+  size_t head_dim = 128;
+  size_t intermediate_size = 4096;
+  size_t h_cycles = 2;
+  size_t l_cycles = 3;
+  size_t n_layers = 16;
+  size_t max_seq_len = 4096;
+  size_t vocab_size = 65536;
+  float rope_theta = 10000.0f;
+  float norm_eps = 1e-6f;
+  float init_std = 0.025515518153991442f;  // 1 / sqrt(1536)
+  float embedding_scale = 39.191835884530846f;
+};
+
+// Owned device allocation of `len` elements of T (cudarc CudaSlice<T>).
+template <class T>
+class CudaSlice {
+ public:
+  CudaSlice() = default;
+  CudaSlice(T* ptr, size_t len) : ptr_(ptr), len_(len) {}
+  CudaSlice(const CudaSlice&) = delete;
+  CudaSlice& operator=(const CudaSlice&) = delete;
+  CudaSlice(CudaSlice&& o) noexcept : ptr_(o.ptr_), len_(o.len_) { o.ptr_ = nullptr; o.len_ = 0; }
+  CudaSlice& operator=(CudaSlice&& o) noexcept {
+    if (this != &o) { reset(); ptr_ = o.ptr_; len_ = o.len_; o.ptr_ = nullptr; o.len_ = 0; }
+    return *this;
+  }
+  ~CudaSlice() { reset(); }
+  T* device_ptr() const { return ptr_; }
+  size_t len() const { return len_; }
+
+ private:
+  void reset() { if (ptr_) cudaFree(ptr_); ptr_ = nullptr; len_ = 0; }
+  T* ptr_ = nullptr;
+  size_t len_ = 0;
+};
+
+class HrmLayerOps {
+ public:
+  // CudaDevice::new(dev_ordinal) + a stream (src/lib.rs:185-186).
+  explicit HrmLayerOps(int dev_ordinal, HrmConfig config = HrmConfig());
+  ~HrmLayerOps();
+  HrmLayerOps(const HrmLayerOps&) = delete;
+  HrmLayerOps& operator=(const HrmLayerOps&) = delete;
+
+  HrmConfig config;
+
+  // ---- buffers (src/lib.rs:258-267 and cudarc's htod_copy / sync_reclaim)
+  CudaSlice<bf16> alloc_zero_bf16(size_t len) const;
+  CudaSlice<bf16> htod_copy_bf16(const std::vector<bf16>& host) const;
+  CudaSlice<uint32_t> htod_copy_u32(const std::vector<uint32_t>& host) const;
+  std::vector<bf16> sync_reclaim(CudaSlice<bf16>&& slice) const;  // waits for the stream
+  cudaStream_t cu_stream() const { return stream_; }
+
+  // ---- the kernel wrappers (same signatures as src/lib.rs:378-565)
+  void additive_inject(const CudaSlice<bf16>& z_a, const CudaSlice<bf16>& z_b, CudaSlice<bf16>& z_out,
+                       size_t total_elements) const;
+  void rms_norm(const CudaSlice<bf16>& input, CudaSlice<bf16>& output, size_t rows, size_t hidden_size) const;
+  void rope_embed(CudaSlice<bf16>& q, CudaSlice<bf16>& k, size_t batch_size, size_t num_heads, size_t seq_len,
+                  size_t head_dim, size_t position_offset) const;
+  void swiglu_ffn(const CudaSlice<bf16>& gate, const CudaSlice<bf16>& up, CudaSlice<bf16>& output,
+                  size_t total_elements) const;
+  void embedding_lookup(const CudaSlice<uint32_t>& input_ids, const CudaSlice<bf16>& embedding_table,
+                        CudaSlice<bf16>& output, size_t batch_size, size_t seq_len, size_t hidden_size,
+                        size_t vocab_size, float embedding_scale) const;
+
+  // ---- fused entry points that replace wrapper sequences of the reference
+  // additive_inject -> rms_norm (src/lib.rs:976-979); weight may be null.
+  void add_rms_norm(const CudaSlice<bf16>& x, const CudaSlice<bf16>& branch, CudaSlice<bf16>& residual_out,
+                    CudaSlice<bf16>& normed_out, const CudaSlice<bf16>* weight, size_t rows,
+                    size_t hidden_size) const;
+  // embedding_lookup -> rms_norm (src/lib.rs:1191-1200, 969); hidden_out may be null.
+  void embed_rms_norm(const CudaSlice<uint32_t>& input_ids, const CudaSlice<bf16>& embedding_table,
+                      CudaSlice<bf16>* hidden_out, CudaSlice<bf16>& normed_out, const CudaSlice<bf16>* weight,
+                      size_t rows, size_t hidden_size, size_t vocab_size, float embedding_scale) const;
+  // Builds the fp32 cos/sin table for config.head_dim / config.rope_theta
+  // covering positions [0, max_positions); rope_embed uses it from then on
+  // for every call it covers, and evaluates angles in-kernel otherwise.
+  void build_rope_table(size_t max_positions);
+
+ private:
+  void check(int status, const char* op) const;
+  int dev_ = 0;
+  cudaStream_t stream_ = nullptr;
+  CudaSlice<float> rope_table_;
+  size_t rope_positions_ = 0;
+};
+
+}  // namespace hrm

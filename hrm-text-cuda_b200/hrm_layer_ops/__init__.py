@@ -1,0 +1,29 @@
+"""sm_100a per-token layer operators of the HRM-Text forward pass.
+
+Python front end of libhrm_ops.so (C ABI: include/hrm_ops.h).  Importing this
+package loads the library and fails loudly when it has not been built.
+"""
+
+from ._lib import HrmError, LIB, LIB_PATH  # noqa: F401
+from .ops import (  # noqa: F401
+    add_rms_norm,
+    additive_inject,
+    embed_rms_norm,
+    embedding_lookup,
+    rms_norm,
+    rope_embed,
+    rope_table,
+    swiglu_ffn,
+)
+
+__all__ = [
+    "HrmError",
+    "additive_inject",
+    "swiglu_ffn",
+    "rms_norm",
+    "add_rms_norm",
+    "rope_table",
+    "rope_embed",
+    "embedding_lookup",
+    "embed_rms_norm",
+]

@@ -1,0 +1,194 @@
+"""PyTorch-tensor front end of the C ABI (one function per hrm_* entry point).
+
+Tensors supply device memory and the stream; every operator runs in
+libhrm_ops.so.  Inputs must be contiguous CUDA tensors; a CPU tensor is an
+error, never a silent fallback.  By default work is queued on the current
+torch stream of the tensors' device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from ._lib import call
+
+_vp = ctypes.c_void_p
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[ctypes.c_void_p]:
+    return None if t is None else _vp(t.data_ptr())
+
+
+def _stream(t: torch.Tensor, stream: Optional[torch.cuda.Stream]) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream(t.device)
+    return _vp(s.cuda_stream)
+
+
+def _need(t: torch.Tensor, name: str, dtypes=(torch.bfloat16,)) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU implementation)")
+    if t.dtype not in dtypes:
+        raise TypeError(f"{name} has dtype {t.dtype}, expected one of {dtypes}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _ids(t: torch.Tensor, name: str) -> None:
+    _need(t, name, (torch.int32, torch.uint32))
+
+
+def additive_inject(z_a: torch.Tensor, z_b: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+                    stream=None) -> torch.Tensor:
+    """out = z_a + z_b (bf16, fp32 add, RNE).  src/lib.rs:378-399."""
+    _need(z_a, "z_a"); _need(z_b, "z_b")
+    if z_a.numel() != z_b.numel():
+        raise ValueError("z_a and z_b differ in size")
+    out = torch.empty_like(z_a) if out is None else out
+    _need(out, "out")
+    if out.numel() != z_a.numel():
+        raise ValueError("out has the wrong size")
+    call("hrm_additive_inject", _ptr(z_a), _ptr(z_b), _ptr(out), z_a.numel(), _stream(z_a, stream))
+    return out
+
+
+def swiglu_ffn(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+               stream=None) -> torch.Tensor:
+    """out = silu(gate) * up (bf16 I/O, fp32 math).  src/lib.rs:483-504."""
+    _need(gate, "gate"); _need(up, "up")
+    if gate.numel() != up.numel():
+        raise ValueError("gate and up differ in size")
+    out = torch.empty_like(gate) if out is None else out
+    _need(out, "out")
+    if out.numel() != gate.numel():
+        raise ValueError("out has the wrong size")
+    call("hrm_swiglu_ffn", _ptr(gate), _ptr(up), _ptr(out), gate.numel(), _stream(gate, stream))
+    return out
+
+
+def _rows(x: torch.Tensor) -> Tuple[int, int]:
+    hidden = x.shape[-1] if x.dim() > 0 else 0
+    return (x.numel() // hidden if hidden else 0), hidden
+
+
+def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None, eps: float = 1e-6,
+             out: Optional[torch.Tensor] = None, *, stream=None) -> torch.Tensor:
+    """RMSNorm over the last dim; bf16 or fp32 I/O (weight of the same dtype or None).
+
+    src/lib.rs:401-422 (bf16, weight None is the reference's parameterless form).
+    """
+    _need(x, "x", (torch.bfloat16, torch.float32))
+    rows, hidden = _rows(x)
+    if weight is not None:
+        _need(weight, "weight", (x.dtype,))
+        if weight.numel() != hidden:
+            raise ValueError("weight must have hidden_size elements")
+    out = torch.empty_like(x) if out is None else out
+    _need(out, "out", (x.dtype,))
+    if out.numel() != x.numel():
+        raise ValueError("out has the wrong size")
+    fn = "hrm_rms_norm" if x.dtype == torch.bfloat16 else "hrm_rms_norm_f32"
+    call(fn, _ptr(x), _ptr(out), _ptr(weight), rows, hidden, eps, _stream(x, stream))
+    return out
+
+
+def add_rms_norm(x: torch.Tensor, branch: torch.Tensor, weight: Optional[torch.Tensor] = None,
+                 eps: float = 1e-6, residual_out: Optional[torch.Tensor] = None,
+                 normed_out: Optional[torch.Tensor] = None, *, stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(r, y) = (x + branch, rms_norm(x + branch) [* weight]) in one pass (bf16).
+
+    Replaces additive_inject -> rms_norm (src/lib.rs:976-979).
+    """
+    _need(x, "x"); _need(branch, "branch")
+    if x.shape != branch.shape:
+        raise ValueError("x and branch differ in shape")
+    rows, hidden = _rows(x)
+    if weight is not None:
+        _need(weight, "weight")
+        if weight.numel() != hidden:
+            raise ValueError("weight must have hidden_size elements")
+    residual_out = torch.empty_like(x) if residual_out is None else residual_out
+    normed_out = torch.empty_like(x) if normed_out is None else normed_out
+    _need(residual_out, "residual_out"); _need(normed_out, "normed_out")
+    if residual_out.numel() != x.numel() or normed_out.numel() != x.numel():
+        raise ValueError("outputs have the wrong size")
+    call("hrm_add_rms_norm", _ptr(x), _ptr(branch), _ptr(residual_out), _ptr(normed_out), _ptr(weight), rows,
+         hidden, eps, _stream(x, stream))
+    return residual_out, normed_out
+
+
+def rope_table(max_positions: int, head_dim: int, theta: float = 10000.0,
+               device: Optional[torch.device] = None, *, stream=None) -> torch.Tensor:
+    """fp32 [max_positions, head_dim] table: cos in [:, :hd/2], sin in [:, hd/2:]."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    table = torch.empty((max_positions, head_dim), dtype=torch.float32, device=device)
+    call("hrm_rope_table_build", _ptr(table), max_positions, head_dim, theta, _stream(table, stream))
+    return table
+
+
+def rope_embed(q: torch.Tensor, k: torch.Tensor, position_offset: int = 0, theta: float = 10000.0,
+               table: Optional[torch.Tensor] = None, *, stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """In-place rotate-half RoPE on q, k of shape [batch, heads, seq, head_dim].
+
+    table=None evaluates angles in-kernel; otherwise a rope_table(...) with at
+    least position_offset + seq rows.  src/lib.rs:424-458.
+    """
+    _need(q, "q"); _need(k, "k")
+    if q.dim() != 4 or q.shape != k.shape:
+        raise ValueError("q and k must both be [batch, heads, seq, head_dim]")
+    b, h, s, d = q.shape
+    positions = 0
+    if table is not None:
+        _need(table, "table", (torch.float32,))
+        if table.dim() != 2 or table.shape[1] != d:
+            raise ValueError("table must be [positions, head_dim]")
+        positions = table.shape[0]
+    call("hrm_rope_embed", _ptr(q), _ptr(k), b, h, s, d, position_offset, theta, _ptr(table), positions,
+         _stream(q, stream))
+    return q, k
+
+
+def embedding_lookup(ids: torch.Tensor, table: torch.Tensor, embedding_scale: float,
+                     out: Optional[torch.Tensor] = None, *, stream=None) -> torch.Tensor:
+    """out[..., :] = table[clamp(ids)] * scale (bit-exact).  src/lib.rs:529-565."""
+    _ids(ids, "ids"); _need(table, "table")
+    if table.dim() != 2:
+        raise ValueError("table must be [vocab, hidden]")
+    vocab, hidden = table.shape
+    out = torch.empty((*ids.shape, hidden), dtype=table.dtype, device=table.device) if out is None else out
+    _need(out, "out")
+    if out.numel() != ids.numel() * hidden:
+        raise ValueError("out has the wrong size")
+    call("hrm_embedding_lookup", _ptr(ids), _ptr(table), _ptr(out), 1, ids.numel(), hidden, vocab,
+         embedding_scale, _stream(table, stream))
+    return out
+
+
+def embed_rms_norm(ids: torch.Tensor, table: torch.Tensor, embedding_scale: float,
+                   weight: Optional[torch.Tensor] = None, eps: float = 1e-6, hidden_out: Optional[torch.Tensor] = None,
+                   normed_out: Optional[torch.Tensor] = None, keep_hidden: bool = True,
+                   *, stream=None) -> Tuple[Optional[torch.Tensor], torch.Tensor]:
+    """(h, y) = (embedding_lookup(ids), rms_norm(h) [* weight]) in one pass.
+
+    keep_hidden=False skips storing h (returns None for it).
+    """
+    _ids(ids, "ids"); _need(table, "table")
+    vocab, hidden = table.shape
+    shape = (*ids.shape, hidden)
+    if hidden_out is None and keep_hidden:
+        hidden_out = torch.empty(shape, dtype=table.dtype, device=table.device)
+    normed_out = torch.empty(shape, dtype=table.dtype, device=table.device) if normed_out is None else normed_out
+    if hidden_out is not None:
+        _need(hidden_out, "hidden_out")
+    _need(normed_out, "normed_out")
+    if weight is not None:
+        _need(weight, "weight")
+        if weight.numel() != hidden:
+            raise ValueError("weight must have hidden_size elements")
+    call("hrm_embed_rms_norm", _ptr(ids), _ptr(table), _ptr(hidden_out), _ptr(normed_out), _ptr(weight),
+         ids.numel(), hidden, vocab, embedding_scale, eps, _stream(table, stream))
+    return hidden_out, normed_out

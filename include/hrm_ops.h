@@ -1,0 +1,153 @@
+/*
+ * hrm_ops.h -- C ABI of the sm_100a per-token layer operators for the
+ * HRM-Text forward/decode loop (ArjavDesa912/hrm-text-cuda).
+ *
+ * Every entry point replaces one launch wrapper of `HrmForwardPass` in the
+ * reference's src/lib.rs (cited per function) together with the PTX kernel
+ * that wrapper loaded (src/kernels/<name>.cu).  The functions are:
+ *   - stateless: no allocation, no free, no host synchronisation;
+ *   - stream ordered: work is queued on `stream` (NULL = the legacy default
+ *     stream of the current device) in the caller's current CUDA context,
+ *     which is the device primary context that cudarc binds;
+ *   - reentrant: the only globals are per-device launch tuning values that
+ *     are written once (SM count), so calls from several host threads on
+ *     different streams are safe.
+ * Device pointers are plain addresses (cudarc: `*slice.device_ptr()`).
+ * bf16 tensors are passed as `void*` holding IEEE bfloat16 (the top 16 bits
+ * of a binary32), row-major.  Sizes are int64_t element counts.
+ *
+ * Return value: HRM_OK (0) or one of the hrm_status codes below; a CUDA
+ * launch failure is reported as HRM_ERR_CUDA + cudaError_t.  Nothing here
+ * traps or aborts, and no call leaves work half-queued on an argument error
+ * (arguments are checked before anything is launched).
+ */
+#ifndef HRM_OPS_H
+#define HRM_OPS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t and CUstream (cudarc: `*dev.cu_stream()`). */
+typedef struct CUstream_st* hrm_stream_t;
+
+enum hrm_status {
+  HRM_OK = 0,
+  HRM_ERR_NULL_POINTER = 1,   /* a required pointer is NULL                     */
+  HRM_ERR_INVALID_SHAPE = 2,  /* negative size, odd head_dim, hidden == 0, ...   */
+  HRM_ERR_SIZE_OVERFLOW = 3,  /* a product of sizes overflows int64 / grid limits */
+  HRM_ERR_ALIASING = 4,       /* buffers that must be distinct overlap           */
+  HRM_ERR_TABLE_RANGE = 5,    /* position_offset + seq_len exceeds the rope table */
+  HRM_ERR_CUDA = 1000         /* HRM_ERR_CUDA + cudaError_t of the failed launch  */
+};
+
+/* Human-readable text for a status code (static storage, never NULL). */
+const char* hrm_status_string(int status);
+
+/* ABI version: major * 10000 + minor * 100 + patch. */
+int hrm_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Residual add.  z_out[i] = bf16_rn(f32(z_a[i]) + f32(z_b[i])), i < n.
+ * Replaces HrmForwardPass::additive_inject (src/lib.rs:378-399) and
+ * additive_inject_kernel_vec8 (src/kernels/additive_inject.cu:6-44).
+ * z_out may alias z_a or z_b exactly (elementwise, in place is fine).      */
+int hrm_additive_inject(const void* z_a, const void* z_b, void* z_out,
+                        int64_t total_elements, hrm_stream_t stream);
+
+/* RMSNorm over the last dim of a row-major [rows, hidden_size] bf16 tensor:
+ *   ss  = sum_j f32(x_j)^2   (fp32, the reference's 256-thread order)
+ *   inv = 1 / sqrtf(ss / hidden_size + eps)
+ *   y_j = bf16_rn(f32(x_j) * inv)            weight == NULL (reference form)
+ *   y_j = bf16_rn((f32(x_j) * inv) * f32(w_j))   weight = bf16 [hidden_size]
+ * Replaces HrmForwardPass::rms_norm (src/lib.rs:401-422; eps was read from
+ * config.norm_eps there and is explicit here) and rms_norm_kernel
+ * (src/kernels/rms_norm.cu:8-66).  output must not overlap input.          */
+int hrm_rms_norm(const void* input, void* output, const void* weight,
+                 int64_t rows, int64_t hidden_size, float eps,
+                 hrm_stream_t stream);
+
+/* fp32-I/O RMSNorm (same formula, fp32 x / w / y).  No reference
+ * counterpart: it serves fp32 activations with the same reduction order as
+ * rms_norm_kernel (src/kernels/rms_norm.cu:25-59).                         */
+int hrm_rms_norm_f32(const float* input, float* output, const float* weight,
+                     int64_t rows, int64_t hidden_size, float eps,
+                     hrm_stream_t stream);
+
+/* Fused residual add + RMSNorm (one HBM pass):
+ *   r = bf16_rn(f32(x) + f32(branch))  -> residual_out
+ *   y = rms_norm(r) [* weight]         -> normed_out  (statistics from the
+ *                                         bf16-rounded r, as when the
+ *                                         reference reads r back from HBM)
+ * Replaces the pair additive_inject -> rms_norm of src/lib.rs:976-979 and
+ * src/lib.rs:1015-1028 + 969.  residual_out may alias x or branch exactly;
+ * normed_out must not overlap any other buffer.                             */
+int hrm_add_rms_norm(const void* x, const void* branch, void* residual_out,
+                     void* normed_out, const void* weight, int64_t rows,
+                     int64_t hidden_size, float eps, hrm_stream_t stream);
+
+/* Rotary embedding, in place on q and k, layout [batch, heads, seq, head_dim]
+ * bf16, rotate-half (NeoX) pairing (x[i], x[i + head_dim/2]):
+ *   a  = (float)(s + position_offset) * expf((-2.0f*i*logf(theta))/head_dim)
+ *   x0' = x0*cos(a) - x1*sin(a);  x1' = x1*cos(a) + x0*sin(a)
+ * rope_table == NULL: angles are evaluated in-kernel with exactly that fp32
+ * formula (as src/kernels/rope_embed.cu:41-43 does).  Otherwise rope_table
+ * is an fp32 table written by hrm_rope_table_build for the same head_dim and
+ * theta, with table_positions rows; position_offset + seq_len must not
+ * exceed table_positions.  Replaces HrmForwardPass::rope_embed
+ * (src/lib.rs:424-458; theta was config.rope_theta there) and
+ * rope_embed_kernel (src/kernels/rope_embed.cu:12-54).  q and k must not
+ * overlap.  head_dim must be even.                                          */
+int hrm_rope_embed(void* q, void* k, int64_t batch_size, int64_t num_heads,
+                   int64_t seq_len, int64_t head_dim, int64_t position_offset,
+                   float theta, const float* rope_table,
+                   int64_t table_positions, hrm_stream_t stream);
+
+/* Writes the fp32 cos/sin table used by hrm_rope_embed:
+ *   table[p * head_dim + i]            = cos(a(p, i)),
+ *   table[p * head_dim + head_dim/2 + i] = sin(a(p, i)),  p < max_positions,
+ * with a(p, i) the angle formula above at s + position_offset = p.  The
+ * table has max_positions * head_dim floats.  No reference counterpart
+ * (the reference evaluates the angle per element); build it once per
+ * (head_dim, theta, max_positions), e.g. next to ScratchBuffers.            */
+int hrm_rope_table_build(float* table, int64_t max_positions,
+                         int64_t head_dim, float theta, hrm_stream_t stream);
+
+/* SwiGLU gate: out[i] = bf16_rn((g * (1 / (1 + exp(-g)))) * u), g = f32(gate[i]),
+ * u = f32(up[i]), exp evaluated by the __expf intrinsic as in the reference.
+ * Replaces HrmForwardPass::swiglu_ffn (src/lib.rs:483-504) and
+ * swiglu_ffn_kernel (src/kernels/swiglu_ffn.cu:9-47).  output may alias
+ * gate or up exactly.                                                       */
+int hrm_swiglu_ffn(const void* gate, const void* up, void* output,
+                   int64_t total_elements, hrm_stream_t stream);
+
+/* Token-embedding gather:
+ *   id' = id >= vocab_size ? vocab_size - 1 : id
+ *   out[t, j] = bf16_rn(f32(table[id', j]) * embedding_scale)
+ * for t < batch_size * seq_len (ids row-major [batch, seq]).  Bit-exact with
+ * the reference.  Replaces HrmForwardPass::embedding_lookup
+ * (src/lib.rs:529-565) and embedding_lookup_kernel
+ * (src/kernels/embedding_lookup.cu:10-51).  Any hidden_size is accepted (the
+ * reference kernel needs hidden_size % 8 == 0).                            */
+int hrm_embedding_lookup(const uint32_t* input_ids, const void* embedding_table,
+                         void* output, int64_t batch_size, int64_t seq_len,
+                         int64_t hidden_size, int64_t vocab_size,
+                         float embedding_scale, hrm_stream_t stream);
+
+/* Fused embedding gather + RMSNorm (one pass over the gathered rows):
+ *   h = embedding_lookup(...)          -> hidden_out (may be NULL: not stored)
+ *   y = rms_norm(h) [* weight]         -> normed_out
+ * Replaces embedding_lookup (src/lib.rs:1191-1200) followed by the first
+ * rms_norm on the same rows (src/lib.rs:969).                               */
+int hrm_embed_rms_norm(const uint32_t* input_ids, const void* embedding_table,
+                       void* hidden_out, void* normed_out, const void* weight,
+                       int64_t rows, int64_t hidden_size, int64_t vocab_size,
+                       float embedding_scale, float eps, hrm_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* HRM_OPS_H */

@@ -1,0 +1,215 @@
+/*
+ * hrm_oracle.c -- test-only CPU restatement of the reference kernels (see
+ * hrm_oracle.h).  Each function cites the reference lines it restates.
+ * OpenMP parallelises over rows / elements only; the arithmetic of each
+ * element is sequential and independent of the thread count.
+ */
+#include "hrm_oracle.h"
+
+#include <math.h>
+#include <omp.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define REF_THREADS 256 /* rms_norm launch: block = 256 (src/lib.rs:408-417) */
+
+uint16_t ora_f32_to_bf16(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fffu; /* canonical NaN */
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+float ora_bf16_to_f32(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+int ora_max_threads(void) { return omp_get_max_threads(); }
+void ora_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+}
+
+/* additive_inject.cu:26-31: fa + fb in fp32, then RNE. */
+void ora_additive_inject(const uint16_t* a, const uint16_t* b, uint16_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) out[i] = ora_f32_to_bf16(ora_bf16_to_f32(a[i]) + ora_bf16_to_f32(b[i]));
+}
+
+/* swiglu_ffn.cu:31-35: sig = 1/(1+exp(-g)); out = (g*sig)*u. */
+void ora_swiglu_ffn(const uint16_t* gate, const uint16_t* up, uint16_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    const float g = ora_bf16_to_f32(gate[i]), u = ora_bf16_to_f32(up[i]);
+    const float sig = 1.0f / (1.0f + expf(-g));
+    out[i] = ora_f32_to_bf16(g * sig * u);
+  }
+}
+
+/*
+ * Sum of squares of one row in the order rms_norm_kernel produces it
+ * (rms_norm.cu:25-56): thread t of 256 accumulates v[t], v[t+256], ... with a
+ * fused multiply-add (nvcc contracts `local_sum += v * v`); a shuffle-down
+ * tree with offsets 16..1 in each warp; the 8 warp sums reduced by a
+ * shuffle-down tree with offsets 4, 2, 1.  Only lane 0's value survives in
+ * each tree, so each level is "x[m] += x[m + off] for m < off".
+ */
+static float ref_sum_squares(const float* v, int64_t hidden) {
+  float part[REF_THREADS];
+  for (int t = 0; t < REF_THREADS; ++t) {
+    float s = 0.0f;
+    for (int64_t i = t; i < hidden; i += REF_THREADS) s = fmaf(v[i], v[i], s);
+    part[t] = s;
+  }
+  float warp_sum[REF_THREADS / 32];
+  for (int w = 0; w < REF_THREADS / 32; ++w) {
+    float* x = part + 32 * w;
+    for (int off = 16; off > 0; off >>= 1)
+      for (int m = 0; m < off; ++m) x[m] = x[m] + x[m + off];
+    warp_sum[w] = x[0];
+  }
+  for (int off = (REF_THREADS / 32) / 2; off > 0; off >>= 1)
+    for (int m = 0; m < off; ++m) warp_sum[m] = warp_sum[m] + warp_sum[m + off];
+  return warp_sum[0];
+}
+
+/* rms_norm.cu:58-59 */
+static float ref_inv_rms(float ss, int64_t hidden, float eps) {
+  const float rms = sqrtf(ss / (float)hidden + eps);
+  return 1.0f / rms;
+}
+
+/* Normalises one row already converted to fp32 (v) into bf16 y. */
+static void norm_row_bf16(const float* v, uint16_t* y, const uint16_t* w, int64_t hidden, float eps) {
+  const float inv = ref_inv_rms(ref_sum_squares(v, hidden), hidden, eps);
+  for (int64_t i = 0; i < hidden; ++i) {
+    float o = v[i] * inv; /* rms_norm.cu:64 */
+    if (w) o = o * ora_bf16_to_f32(w[i]);
+    y[i] = ora_f32_to_bf16(o);
+  }
+}
+
+void ora_rms_norm(const uint16_t* x, uint16_t* y, const uint16_t* w, int64_t rows, int64_t hidden, float eps) {
+#pragma omp parallel
+  {
+    float* v = (float*)malloc((size_t)hidden * sizeof(float));
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      for (int64_t i = 0; i < hidden; ++i) v[i] = ora_bf16_to_f32(x[r * hidden + i]);
+      norm_row_bf16(v, y + r * hidden, w, hidden, eps);
+    }
+    free(v);
+  }
+}
+
+void ora_rms_norm_f32(const float* x, float* y, const float* w, int64_t rows, int64_t hidden, float eps) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* v = x + r * hidden;
+    const float inv = ref_inv_rms(ref_sum_squares(v, hidden), hidden, eps);
+    for (int64_t i = 0; i < hidden; ++i) {
+      float o = v[i] * inv;
+      if (w) o = o * w[i];
+      y[r * hidden + i] = o;
+    }
+  }
+}
+
+/* additive_inject (additive_inject.cu:29-31) then rms_norm of the rounded sum. */
+void ora_add_rms_norm(const uint16_t* x, const uint16_t* branch, uint16_t* residual, uint16_t* normed,
+                      const uint16_t* w, int64_t rows, int64_t hidden, float eps) {
+#pragma omp parallel
+  {
+    float* v = (float*)malloc((size_t)hidden * sizeof(float));
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      for (int64_t i = 0; i < hidden; ++i) {
+        const int64_t e = r * hidden + i;
+        const uint16_t s = ora_f32_to_bf16(ora_bf16_to_f32(x[e]) + ora_bf16_to_f32(branch[e]));
+        residual[e] = s;
+        v[i] = ora_bf16_to_f32(s);
+      }
+      norm_row_bf16(v, normed + r * hidden, w, hidden, eps);
+    }
+    free(v);
+  }
+}
+
+/* embedding_lookup.cu:33-35 */
+static int64_t clamp_id(uint32_t id, int64_t vocab) { return id >= (uint32_t)vocab ? vocab - 1 : (int64_t)id; }
+
+/* embedding_lookup.cu:37-50: one fp32 multiply, RNE. */
+void ora_embedding_lookup(const uint32_t* ids, const uint16_t* table, uint16_t* out, int64_t tokens, int64_t hidden,
+                          int64_t vocab, float scale) {
+#pragma omp parallel for schedule(static)
+  for (int64_t t = 0; t < tokens; ++t) {
+    const uint16_t* row = table + clamp_id(ids[t], vocab) * hidden;
+    for (int64_t j = 0; j < hidden; ++j) out[t * hidden + j] = ora_f32_to_bf16(ora_bf16_to_f32(row[j]) * scale);
+  }
+}
+
+void ora_embed_rms_norm(const uint32_t* ids, const uint16_t* table, uint16_t* hidden_out, uint16_t* normed,
+                        const uint16_t* w, int64_t rows, int64_t hidden, int64_t vocab, float scale, float eps) {
+#pragma omp parallel
+  {
+    float* v = (float*)malloc((size_t)hidden * sizeof(float));
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      const uint16_t* row = table + clamp_id(ids[r], vocab) * hidden;
+      for (int64_t j = 0; j < hidden; ++j) {
+        const uint16_t h = ora_f32_to_bf16(ora_bf16_to_f32(row[j]) * scale);
+        if (hidden_out) hidden_out[r * hidden + j] = h;
+        v[j] = ora_bf16_to_f32(h);
+      }
+      norm_row_bf16(v, normed + r * hidden, w, hidden, eps);
+    }
+    free(v);
+  }
+}
+
+/* rope_embed.cu:41: angle = (pos + offset) * exp(((-2*i) * log(theta)) / head_dim). */
+static float rope_angle(int pos, int i, int head_dim, float theta) {
+  return (float)pos * expf(-2.0f * i * logf(theta) / (float)head_dim);
+}
+
+void ora_rope_table(float* table, int64_t positions, int64_t head_dim, float theta) {
+  const int64_t half = head_dim / 2;
+#pragma omp parallel for schedule(static)
+  for (int64_t p = 0; p < positions; ++p)
+    for (int64_t i = 0; i < half; ++i) {
+      const float a = rope_angle((int)p, (int)i, (int)head_dim, theta);
+      table[p * head_dim + i] = cosf(a);
+      table[p * head_dim + half + i] = sinf(a);
+    }
+}
+
+/* rope_embed.cu:27-53: pair (i, i + D/2) of row (b, h, s), Q then K. */
+void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                    int64_t offset, float theta, const float* table) {
+  const int64_t half = head_dim / 2, rows = batch * heads * seq;
+#pragma omp parallel for schedule(static)
+  for (int64_t row = 0; row < rows; ++row) {
+    const int pos = (int)(row % seq) + (int)offset;
+    for (int64_t i = 0; i < half; ++i) {
+      float c, s;
+      if (table) {
+        c = table[(int64_t)pos * head_dim + i];
+        s = table[(int64_t)pos * head_dim + half + i];
+      } else {
+        const float a = rope_angle(pos, (int)i, (int)head_dim, theta);
+        c = cosf(a);
+        s = sinf(a);
+      }
+      const int64_t i0 = row * head_dim + i, i1 = i0 + half;
+      const float x0 = ora_bf16_to_f32(q[i0]), x1 = ora_bf16_to_f32(q[i1]);
+      q[i0] = ora_f32_to_bf16(x0 * c - x1 * s);
+      q[i1] = ora_f32_to_bf16(x1 * c + x0 * s);
+      const float k0 = ora_bf16_to_f32(k[i0]), k1 = ora_bf16_to_f32(k[i1]);
+      k[i0] = ora_f32_to_bf16(k0 * c - k1 * s);
+      k[i1] = ora_f32_to_bf16(k1 * c + k0 * s);
+    }
+  }
+}

@@ -1,0 +1,64 @@
+// Test-only harness around the reference's own kernels, compiled from the
+// reference sources where they lie (oracle/Makefile passes -I to
+// src/kernels of the reference checkout) into oracle/_ref/libref_kernels.so.
+// Each ref_* function launches one reference kernel with the launch
+// configuration its wrapper in src/lib.rs computes, so the GPU tests can pin
+// the CPU oracle -- and this project's kernels -- against the reference
+// itself, and time it on the same GPU.  Returns the cudaError_t of the launch.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "additive_inject.cu"
+#include "embedding_lookup.cu"
+#include "rms_norm.cu"
+#include "rope_embed.cu"
+#include "swiglu_ffn.cu"
+
+namespace {
+unsigned blocks_for(int64_t work, int64_t threads) { return (unsigned)((work + threads - 1) / threads); }
+}  // namespace
+
+extern "C" {
+
+// src/lib.rs:384-396
+int ref_additive_inject(const void* a, const void* b, void* out, int64_t n, cudaStream_t s) {
+  const unsigned blocks = blocks_for((n + 7) / 8, 256);
+  additive_inject_kernel_vec8<<<blocks, 256, 0, s>>>((const __nv_bfloat16*)a, (const __nv_bfloat16*)b,
+                                                     (__nv_bfloat16*)out, (int)n);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:408-419
+int ref_rms_norm(const void* x, void* y, int64_t rows, int64_t hidden, float eps, cudaStream_t s) {
+  rms_norm_kernel<<<(unsigned)rows, 256, 8 * sizeof(float), s>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)y,
+                                                                 (int)hidden, eps);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:433-455
+int ref_rope_embed(void* q, void* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t offset,
+                   float theta, cudaStream_t s) {
+  const unsigned blocks = blocks_for(batch * heads * seq * (head_dim / 2), 256);
+  rope_embed_kernel<<<blocks, 256, 0, s>>>((__nv_bfloat16*)q, (__nv_bfloat16*)k, (int)batch, (int)heads, (int)seq,
+                                           (int)head_dim, (int)offset, theta);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:489-501
+int ref_swiglu_ffn(const void* g, const void* u, void* out, int64_t n, cudaStream_t s) {
+  const unsigned blocks = blocks_for((n + 7) / 8, 256);
+  swiglu_ffn_kernel<<<blocks, 256, 0, s>>>((const __nv_bfloat16*)g, (const __nv_bfloat16*)u, (__nv_bfloat16*)out,
+                                           (int)n);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:540-562
+int ref_embedding_lookup(const uint32_t* ids, const void* table, void* out, int64_t batch, int64_t seq,
+                         int64_t hidden, int64_t vocab, float scale, cudaStream_t s) {
+  const unsigned blocks = blocks_for(batch * seq * (hidden / 8), 256);
+  embedding_lookup_kernel<<<blocks, 256, 0, s>>>(ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, (int)batch,
+                                                 (int)seq, (int)hidden, (int)vocab, scale);
+  return (int)cudaGetLastError();
+}
+
+}  // extern "C"

@@ -1,0 +1,170 @@
+// Known-answer tests of the C++ host layer, restating the reference's GPU
+// tests (src/lib.rs:2225-2279: test_additive_inject, test_rms_norm,
+// test_swiglu_ffn) through HrmLayerOps, plus known answers for the two ops
+// the reference never tested (embedding_lookup, rope_embed) and the fused
+// entry points.  Needs a GPU; prints one line per test and exits non-zero on
+// the first failure.
+#include <cmath>
+#include <cstdio>
+#include <functional>
+#include <string>
+#include <vector>
+
+#include "hrm_layer_ops.hpp"
+
+using hrm::bf16;
+using hrm::HrmError;
+using hrm::HrmLayerOps;
+
+namespace {
+
+std::vector<bf16> to_bf16(const std::vector<float>& v) {
+  std::vector<bf16> o;
+  for (float x : v) o.push_back(bf16::from_f32(x));
+  return o;
+}
+
+struct Failure {
+  std::string what;
+};
+
+void expect(bool ok, const std::string& what) {
+  if (!ok) throw Failure{what};
+}
+
+// src/lib.rs:2227-2243
+void test_additive_inject(HrmLayerOps& hrm) {
+  auto a = hrm.htod_copy_bf16(to_bf16({1.0f, 2.0f, 3.0f, 4.0f}));
+  auto b = hrm.htod_copy_bf16(to_bf16({0.5f, 1.5f, 2.5f, 3.5f}));
+  auto out = hrm.alloc_zero_bf16(4);
+  hrm.additive_inject(a, b, out, 4);
+  auto host = hrm.sync_reclaim(std::move(out));
+  const float expected[4] = {1.5f, 3.5f, 5.5f, 7.5f};
+  for (int i = 0; i < 4; ++i) expect(std::fabs(host[i].to_f32() - expected[i]) < 0.01f, "additive_inject value");
+}
+
+// src/lib.rs:2247-2261
+void test_rms_norm(HrmLayerOps& hrm) {
+  auto inp = hrm.htod_copy_bf16(to_bf16({1.0f, 2.0f, 3.0f, 4.0f}));
+  auto out = hrm.alloc_zero_bf16(4);
+  hrm.rms_norm(inp, out, 1, 4);
+  auto host = hrm.sync_reclaim(std::move(out));
+  const float rms = std::sqrt(1.0f + 4.0f + 9.0f + 16.0f) / 2.0f;
+  for (int i = 0; i < 4; ++i) expect(std::fabs(host[i].to_f32() - (i + 1) / rms) < 0.01f, "rms_norm value");
+}
+
+// src/lib.rs:2265-2279
+void test_swiglu_ffn(HrmLayerOps& hrm) {
+  auto g = hrm.htod_copy_bf16(to_bf16({0.0f, 0.0f, 0.0f, 0.0f}));
+  auto u = hrm.htod_copy_bf16(to_bf16({2.0f, 2.0f, 2.0f, 2.0f}));
+  auto out = hrm.alloc_zero_bf16(4);
+  hrm.swiglu_ffn(g, u, out, 4);
+  auto host = hrm.sync_reclaim(std::move(out));
+  for (int i = 0; i < 4; ++i) expect(std::fabs(host[i].to_f32()) < 0.01f, "swiglu_ffn value");
+}
+
+// Embedding with scale 1 returns table rows exactly; an id >= vocab reads
+// row vocab-1 (src/kernels/embedding_lookup.cu:35).
+void test_embedding_lookup(HrmLayerOps& hrm) {
+  const size_t vocab = 3, hidden = 8;
+  std::vector<float> t(vocab * hidden);
+  for (size_t i = 0; i < t.size(); ++i) t[i] = 0.25f * (float)i - 1.0f;
+  auto table = hrm.htod_copy_bf16(to_bf16(t));
+  auto ids = hrm.htod_copy_u32({2, 0, 7});
+  auto out = hrm.alloc_zero_bf16(3 * hidden);
+  hrm.embedding_lookup(ids, table, out, 1, 3, hidden, vocab, 1.0f);
+  auto host = hrm.sync_reclaim(std::move(out));
+  const size_t rows[3] = {2, 0, 2};
+  for (size_t r = 0; r < 3; ++r)
+    for (size_t j = 0; j < hidden; ++j)
+      expect(host[r * hidden + j].to_f32() == t[rows[r] * hidden + j], "embedding_lookup row");
+}
+
+// RoPE at position 0 is the identity; at position 1 pair 0 rotates by 1 rad.
+void test_rope_embed(HrmLayerOps& hrm) {
+  const size_t hd = 128, n = 2 * hd;  // batch 1, heads 1, seq 2
+  std::vector<float> v(n);
+  for (size_t i = 0; i < n; ++i) v[i] = (float)((i % 7) + 1) * 0.125f;
+  auto host_in = to_bf16(v);
+  auto q = hrm.htod_copy_bf16(host_in);
+  auto k = hrm.htod_copy_bf16(host_in);
+  hrm.rope_embed(q, k, 1, 1, 2, hd, 0);
+  auto qh = hrm.sync_reclaim(std::move(q));
+  for (size_t i = 0; i < hd; ++i) expect(qh[i].bits == host_in[i].bits, "rope position 0 identity");
+  const float x0 = host_in[hd].to_f32(), x1 = host_in[hd + hd / 2].to_f32();
+  const float e0 = x0 * std::cos(1.0f) - x1 * std::sin(1.0f);
+  expect(std::fabs(qh[hd].to_f32() - e0) < 0.01f, "rope position 1 pair 0");
+}
+
+// Fused add + norm equals additive_inject followed by rms_norm, bit for bit.
+void test_add_rms_norm(HrmLayerOps& hrm) {
+  const size_t rows = 3, hidden = 2048;
+  std::vector<float> a(rows * hidden), b(rows * hidden);
+  for (size_t i = 0; i < a.size(); ++i) {
+    a[i] = std::sin(0.37f * (float)i);
+    b[i] = std::cos(0.11f * (float)i) * 0.5f;
+  }
+  auto da = hrm.htod_copy_bf16(to_bf16(a));
+  auto db = hrm.htod_copy_bf16(to_bf16(b));
+  auto r1 = hrm.alloc_zero_bf16(a.size());
+  auto y1 = hrm.alloc_zero_bf16(a.size());
+  auto r2 = hrm.alloc_zero_bf16(a.size());
+  auto y2 = hrm.alloc_zero_bf16(a.size());
+  hrm.additive_inject(da, db, r1, a.size());
+  hrm.rms_norm(r1, y1, rows, hidden);
+  hrm.add_rms_norm(da, db, r2, y2, nullptr, rows, hidden);
+  auto hr1 = hrm.sync_reclaim(std::move(r1)), hy1 = hrm.sync_reclaim(std::move(y1));
+  auto hr2 = hrm.sync_reclaim(std::move(r2)), hy2 = hrm.sync_reclaim(std::move(y2));
+  for (size_t i = 0; i < a.size(); ++i) {
+    expect(hr1[i].bits == hr2[i].bits, "add_rms_norm residual");
+    expect(hy1[i].bits == hy2[i].bits, "add_rms_norm normed");
+  }
+}
+
+// Argument errors come back as HrmError::InvalidInput, not as a launch.
+void test_invalid_input(HrmLayerOps& hrm) {
+  auto a = hrm.alloc_zero_bf16(4);
+  auto out = hrm.alloc_zero_bf16(4);
+  bool thrown = false;
+  try {
+    hrm.additive_inject(a, a, out, 8);  // slices hold 4 elements
+  } catch (const HrmError& e) {
+    thrown = e.kind() == HrmError::Kind::InvalidInput;
+  }
+  expect(thrown, "short slice rejected");
+  thrown = false;
+  try {
+    hrm.rope_embed(a, out, 1, 1, 1, 3, 0);  // odd head_dim (slices hold 4 >= 3)
+  } catch (const HrmError& e) {
+    thrown = e.kind() == HrmError::Kind::InvalidInput && e.status() == HRM_ERR_INVALID_SHAPE;
+  }
+  expect(thrown, "odd head_dim rejected");
+}
+
+}  // namespace
+
+int main() {
+  const std::vector<std::pair<const char*, std::function<void(HrmLayerOps&)>>> tests = {
+      {"test_additive_inject", test_additive_inject}, {"test_rms_norm", test_rms_norm},
+      {"test_swiglu_ffn", test_swiglu_ffn},           {"test_embedding_lookup", test_embedding_lookup},
+      {"test_rope_embed", test_rope_embed},           {"test_add_rms_norm", test_add_rms_norm},
+      {"test_invalid_input", test_invalid_input},
+  };
+  try {
+    HrmLayerOps hrm(0);
+    for (const auto& t : tests) {
+      try {
+        t.second(hrm);
+      } catch (const Failure& f) {
+        std::printf("FAIL %s: %s\n", t.first, f.what.c_str());
+        return 1;
+      }
+      std::printf("ok   %s\n", t.first);
+    }
+  } catch (const HrmError& e) {
+    std::printf("FAIL HrmError: %s\n", e.what());
+    return 1;
+  }
+  std::printf("all %zu tests passed\n", tests.size());
+  return 0;
+}

@@ -1,0 +1,21 @@
+"""GPU: the C++ host layer's known-answer tests (tests/cpp/test_layer_ops.cpp),
+which restate the reference's own GPU tests (src/lib.rs:2225-2279) through
+the HrmLayerOps methods that mirror the reference's wrappers."""
+
+import os
+import subprocess
+
+import pytest
+
+from conftest import PKG
+
+pytestmark = pytest.mark.gpu
+
+
+def test_cpp_host_known_answers():
+    exe = os.path.join(PKG, "build", "test_layer_ops")
+    assert os.path.exists(exe), "build with make -C hrm-text-cuda_b200"
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    print(res.stdout)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "all 7 tests passed" in res.stdout

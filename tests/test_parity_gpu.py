@@ -1,0 +1,231 @@
+"""GPU parity: every operator through the C ABI against the oracle.
+
+Bars (written per test): bit-exact for the residual add, the embedding gather
+and RMSNorm in all its forms (the kernels reproduce the reference's
+reduction order); <= 2 bf16 ulp for SwiGLU (C-library expf in the oracle vs
+the __expf intrinsic) and RoPE (C-library vs CUDA expf/logf/sincosf; ulp
+measured at the rotated pair's magnitude).  Shapes cover the edge cases the
+reference's launch code meets or mishandles: single rows, tails that are not
+a multiple of the 8-element vector, hidden sizes that are not a multiple of
+8, misaligned pointers (scalar paths), out-of-range ids, in-place calls,
+special values, empty inputs and the fallback paths for large rows.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import hrm_layer_ops as ops
+from helpers import ULP_TOL, assert_bits_equal, normal_bf16, rope_pair_magnitude, to_dev, to_host
+from oracle import f32_to_bf16, ulp_error
+
+pytestmark = pytest.mark.gpu
+
+
+def misaligned(t):
+    """A view of t shifted by one element (2 bytes): not 16-byte aligned."""
+    buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+    v = buf[1:].view(t.shape)
+    v.copy_(t)
+    return v
+
+
+# ------------------------------------------------------------ additive add
+@pytest.mark.parametrize("n", [1, 7, 8, 9, 4096, 65536 + 5, (1 << 20) + 3])
+def test_additive_inject(oracle, rng, cuda, n):
+    a, b = normal_bf16(rng, n, 3.0), normal_bf16(rng, n)
+    out = ops.additive_inject(to_dev(a, cuda), to_dev(b, cuda))
+    assert_bits_equal(to_host(out), oracle.additive_inject(a, b), "additive_inject")
+
+
+def test_additive_inject_in_place_and_misaligned(oracle, rng, cuda):
+    n = 10001
+    a, b = normal_bf16(rng, n), normal_bf16(rng, n)
+    want = oracle.additive_inject(a, b)
+    da = to_dev(a, cuda)
+    ops.additive_inject(da, to_dev(b, cuda), out=da)  # z_out aliases z_a exactly
+    assert_bits_equal(to_host(da), want, "in place")
+    ma, mb = misaligned(to_dev(a, cuda)), misaligned(to_dev(b, cuda))
+    assert_bits_equal(to_host(ops.additive_inject(ma, mb, out=misaligned(torch.empty_like(ma)))), want, "misaligned")
+
+
+# ------------------------------------------------------------------ swiglu
+@pytest.mark.parametrize("n", [1, 4, 7, 8, 9, 1000003, 32 * 5632])
+def test_swiglu(oracle, rng, cuda, n):
+    g, u = normal_bf16(rng, n, 0.5), normal_bf16(rng, n, 0.5)
+    out = to_host(ops.swiglu_ffn(to_dev(g, cuda), to_dev(u, cuda)))
+    err = ulp_error(out, oracle.swiglu_ffn(g, u))
+    assert err.max() <= ULP_TOL, f"max {err.max()} ulp"
+
+
+def test_swiglu_special_values_in_place_misaligned(oracle, rng, cuda):
+    g = np.array([0x0000, 0x8000, 0x7F80, 0xFF80, 0x7FC0, 0x4300, 0xC300, 0x0001, 0x42F0, 0xC2F0, 0x3F80],
+                 np.uint16)  # 0, -0, inf, -inf, nan, 128, -128, denormal, 120, -120, 1
+    u = f32_to_bf16(np.array([2.0, 2.0, 1.0, 1.0, 1.0, 1.0, 1.0, 1e30, 3.0, 3.0, -1.0], np.float32))
+    want = oracle.swiglu_ffn(g, u)
+    for dg, du in ((to_dev(g, cuda), to_dev(u, cuda)), (misaligned(to_dev(g, cuda)), misaligned(to_dev(u, cuda)))):
+        err = ulp_error(to_host(ops.swiglu_ffn(dg, du)), want)
+        assert err.max() <= ULP_TOL, f"max {err.max()} ulp"
+    g2, u2 = normal_bf16(rng, 4099), normal_bf16(rng, 4099)
+    dg = to_dev(g2, cuda)
+    ops.swiglu_ffn(dg, to_dev(u2, cuda), out=dg)
+    assert ulp_error(to_host(dg), oracle.swiglu_ffn(g2, u2)).max() <= ULP_TOL
+
+
+# ----------------------------------------------------------------- rmsnorm
+NORM_SHAPES = [(1, 4), (1, 8), (3, 24), (7, 1000), (2, 200), (64, 1536), (129, 2048), (5, 4096), (3, 6144),
+               (2, 4100)]
+
+
+@pytest.mark.parametrize("rows,hidden", NORM_SHAPES)
+@pytest.mark.parametrize("with_weight", [False, True])
+def test_rms_norm_bitexact(oracle, rng, cuda, rows, hidden, with_weight):
+    x = normal_bf16(rng, (rows, hidden), 2.0)
+    w = normal_bf16(rng, hidden, 0.1, 1.0) if with_weight else None
+    y = ops.rms_norm(to_dev(x, cuda), None if w is None else to_dev(w, cuda), eps=1e-5)
+    assert_bits_equal(to_host(y), oracle.rms_norm(x, w, eps=1e-5), f"rms_norm {rows}x{hidden}")
+
+
+def test_rms_norm_reference_kat(cuda):
+    """src/lib.rs:2247-2261: rows 1, hidden 4, x = [1, 2, 3, 4]."""
+    x = torch.tensor([[1.0, 2.0, 3.0, 4.0]], dtype=torch.bfloat16, device=cuda)
+    y = ops.rms_norm(x, eps=1e-6).float().cpu().numpy()
+    rms = np.sqrt(30.0) / 2
+    assert np.all(np.abs(y - np.array([1, 2, 3, 4]) / rms) < 0.01)
+
+
+def test_rms_norm_misaligned_and_special_rows(oracle, rng, cuda):
+    x = normal_bf16(rng, (6, 2048))
+    x[1] = 0                         # all-zero row: y = 0
+    x[2, :5] = [0x7F80, 0, 0, 0, 0]  # +inf in a row: ss = inf -> inv = 0, inf * 0 = nan
+    x[3] = f32_to_bf16(np.full(2048, 1e30, np.float32))  # ss overflows fp32
+    want = oracle.rms_norm(x, None, eps=1e-6)
+    assert_bits_equal(to_host(ops.rms_norm(to_dev(x, cuda), eps=1e-6)), want, "special rows")
+    dx = misaligned(to_dev(x, cuda))
+    assert_bits_equal(to_host(ops.rms_norm(dx, eps=1e-6, out=misaligned(torch.empty_like(dx)))), want, "misaligned")
+
+
+def test_rms_norm_empty(cuda):
+    x = torch.empty((0, 2048), dtype=torch.bfloat16, device=cuda)
+    assert ops.rms_norm(x).shape == (0, 2048)
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 4), (33, 2048), (17, 1000), (4, 3000)])
+def test_rms_norm_f32_bitexact(oracle, rng, cuda, rows, hidden):
+    x = rng.standard_normal((rows, hidden)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
+    y = ops.rms_norm(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), eps=1e-5).cpu().numpy()
+    assert np.array_equal(y.view(np.uint32), oracle.rms_norm_f32(x, w, eps=1e-5).view(np.uint32))
+
+
+# ------------------------------------------------------------ add + rmsnorm
+@pytest.mark.parametrize("rows,hidden", [(1, 8), (3, 24), (65, 2048), (9, 1536), (4, 4096), (3, 5000), (2, 12)])
+@pytest.mark.parametrize("with_weight", [False, True])
+def test_add_rms_norm_bitexact(oracle, rng, cuda, rows, hidden, with_weight):
+    x, b = normal_bf16(rng, (rows, hidden)), normal_bf16(rng, (rows, hidden))
+    w = normal_bf16(rng, hidden, 0.1, 1.0) if with_weight else None
+    r, y = ops.add_rms_norm(to_dev(x, cuda), to_dev(b, cuda), None if w is None else to_dev(w, cuda), eps=1e-5)
+    wr, wy = oracle.add_rms_norm(x, b, w, eps=1e-5)
+    assert_bits_equal(to_host(r), wr, "residual")
+    assert_bits_equal(to_host(y), wy, "normed")
+
+
+def test_add_rms_norm_residual_in_place(oracle, rng, cuda):
+    x, b = normal_bf16(rng, (40, 2048)), normal_bf16(rng, (40, 2048))
+    wr, wy = oracle.add_rms_norm(x, b, None, eps=1e-6)
+    for alias in ("x", "branch"):
+        dx, db = to_dev(x, cuda), to_dev(b, cuda)
+        r, y = ops.add_rms_norm(dx, db, eps=1e-6, residual_out=dx if alias == "x" else db)
+        assert_bits_equal(to_host(r), wr, f"residual aliasing {alias}")
+        assert_bits_equal(to_host(y), wy, f"normed aliasing {alias}")
+
+
+# --------------------------------------------------------------- embedding
+@pytest.mark.parametrize("vocab,hidden,tokens", [(10, 8, 5), (100, 24, 33), (32000, 2048, 300), (77, 2052, 9),
+                                                 (50, 5000, 4), (12, 6, 7)])
+@pytest.mark.parametrize("scale", [1.0, 45.254834, 39.191835884530846])
+def test_embedding_bitexact(oracle, rng, cuda, vocab, hidden, tokens, scale):
+    table = normal_bf16(rng, (vocab, hidden), 0.02)
+    ids = rng.integers(0, vocab, tokens, dtype=np.uint32)
+    ids[0] = vocab - 1
+    if tokens > 3:
+        ids[1], ids[2] = vocab, 0xFFFFFFFF  # clamped to vocab - 1
+    out = ops.embedding_lookup(to_dev(ids, cuda), to_dev(table, cuda), scale)
+    assert_bits_equal(to_host(out), oracle.embedding_lookup(ids, table, scale), "embedding")
+
+
+def test_embedding_misaligned_table(oracle, rng, cuda):
+    table = normal_bf16(rng, (40, 64), 0.02)
+    ids = rng.integers(0, 40, 21, dtype=np.uint32)
+    dt = misaligned(to_dev(table, cuda))
+    out = ops.embedding_lookup(to_dev(ids, cuda), dt, 3.0)
+    assert_bits_equal(to_host(out), oracle.embedding_lookup(ids, table, 3.0), "misaligned table")
+
+
+@pytest.mark.parametrize("hidden", [8, 1536, 2048, 4104])
+@pytest.mark.parametrize("keep_hidden", [True, False])
+def test_embed_rms_norm_bitexact(oracle, rng, cuda, hidden, keep_hidden):
+    table = normal_bf16(rng, (500, hidden), 0.02)
+    w = normal_bf16(rng, hidden, 0.1, 1.0)
+    ids = rng.integers(0, 520, 97, dtype=np.uint32)
+    h, y = ops.embed_rms_norm(to_dev(ids, cuda), to_dev(table, cuda), 45.254834, to_dev(w, cuda), eps=1e-5,
+                              keep_hidden=keep_hidden)
+    wh, wy = oracle.embed_rms_norm(ids, table, 45.254834, w, eps=1e-5)
+    assert_bits_equal(to_host(y), wy, "normed")
+    if keep_hidden:
+        assert_bits_equal(to_host(h), wh, "hidden")
+
+
+# -------------------------------------------------------------------- rope
+ROPE_CASES = [(2, 4, 300, 128, 0), (8, 16, 1, 128, 4095), (1, 12, 33, 128, 7), (3, 2, 77, 64, 3),
+              (2, 3, 5, 32, 0), (1, 2, 9, 96, 11), (1, 1, 3, 130, 1), (2, 5, 17, 256, 100), (1, 3, 2, 2, 0)]
+
+
+def check_rope(oracle, q, k, dq, dk, offset, theta):
+    wq, wk = oracle.rope_embed(q, k, offset, theta)
+    for got, want, name in ((to_host(dq), wq, "q"), (to_host(dk), wk, "k")):
+        err = ulp_error(got, want, rope_pair_magnitude(want))
+        assert err.max() <= ULP_TOL, f"{name}: max {err.max()} ulp"
+
+
+@pytest.mark.parametrize("b,h,s,d,off", ROPE_CASES)
+@pytest.mark.parametrize("use_table", [False, True])
+def test_rope(oracle, rng, cuda, b, h, s, d, off, use_table):
+    theta = 10000.0
+    q, k = normal_bf16(rng, (b, h, s, d)), normal_bf16(rng, (b, h, s, d))
+    dq, dk = to_dev(q, cuda), to_dev(k, cuda)
+    table = ops.rope_table(off + s, d, theta) if use_table else None
+    ops.rope_embed(dq, dk, off, theta, table)
+    check_rope(oracle, q, k, dq, dk, off, theta)
+
+
+def test_rope_table_and_in_kernel_angles_agree_bitwise(rng, cuda):
+    q = to_dev(normal_bf16(rng, (2, 16, 512, 128)), cuda)
+    k = to_dev(normal_bf16(rng, (2, 16, 512, 128)), cuda)
+    q1, k1, q2, k2 = q.clone(), k.clone(), q.clone(), k.clone()
+    ops.rope_embed(q1, k1, 1000, 10000.0, None)
+    ops.rope_embed(q2, k2, 1000, 10000.0, ops.rope_table(1512, 128, 10000.0))
+    assert torch.equal(q1.view(torch.int16), q2.view(torch.int16))
+    assert torch.equal(k1.view(torch.int16), k2.view(torch.int16))
+
+
+def test_rope_misaligned(oracle, rng, cuda):
+    q, k = normal_bf16(rng, (1, 4, 20, 128)), normal_bf16(rng, (1, 4, 20, 128))
+    dq, dk = misaligned(to_dev(q, cuda)), misaligned(to_dev(k, cuda))
+    ops.rope_embed(dq, dk, 5, 10000.0, None)
+    check_rope(oracle, q, k, dq, dk, 5, 10000.0)
+
+
+def test_rope_table_close_to_oracle(oracle, cuda):
+    """CUDA's and the C library's expf / sincosf may differ by an fp32 ulp or two;
+    at angle ~4095 rad that is ~5e-4 of the angle."""
+    t = ops.rope_table(4096, 128, 10000.0).cpu().numpy()
+    want = oracle.rope_table(4096, 128, 10000.0)
+    assert np.max(np.abs(t - want)) < 2e-3
+    assert np.array_equal(t[0], want[0])  # position 0: cos 1, sin 0
+
+
+def test_rope_table_range_error(cuda):
+    q = torch.zeros((1, 1, 4, 128), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ops.HrmError):
+        ops.rope_embed(q, q.clone(), 10, 10000.0, ops.rope_table(12, 128))

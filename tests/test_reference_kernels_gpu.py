@@ -1,0 +1,95 @@
+"""GPU: this library against the reference's own kernels, run side by side.
+
+The reference kernels are compiled from the reference's sources
+(oracle/_ref/libref_kernels.so) and launched with its wrappers' launch
+configurations, on the same inputs as this library's kernels.  Where the
+arithmetic is the same instruction for instruction -- residual add, SwiGLU
+(same __expf expression), embedding gather, RMSNorm (same reduction order),
+RoPE (same angle expression, fed through the in-kernel path or the table) --
+the outputs are required to be bit-identical.  The oracle is checked against
+the same reference outputs (bit-exact / <= 2 bf16 ulp), which is what pins
+the oracle to the reference.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import hrm_layer_ops as ops
+from helpers import ULP_TOL, assert_bits_equal, normal_bf16, rope_pair_magnitude, to_dev, to_host
+from oracle import RefKernels, ulp_error
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not RefKernels.available():
+        pytest.fail("oracle/_ref/libref_kernels.so missing: build it where the reference checkout exists")
+    return RefKernels()
+
+
+def test_additive_inject_matches_reference(ref, oracle, rng, cuda):
+    a, b = normal_bf16(rng, 300007), normal_bf16(rng, 300007)
+    da, db = to_dev(a, cuda), to_dev(b, cuda)
+    r = torch.empty_like(da)
+    ref.additive_inject(da, db, r)
+    assert_bits_equal(to_host(ops.additive_inject(da, db)), to_host(r), "vs reference")
+    assert_bits_equal(oracle.additive_inject(a, b), to_host(r), "oracle vs reference")
+
+
+def test_swiglu_matches_reference(ref, oracle, rng, cuda):
+    g, u = normal_bf16(rng, 1 << 20, 0.5), normal_bf16(rng, 1 << 20, 0.5)
+    g[:6] = np.array([0x0000, 0x8000, 0x7F80, 0xFF80, 0x7FC0, 0x0001], np.uint16)
+    dg, du = to_dev(g, cuda), to_dev(u, cuda)
+    r = torch.empty_like(dg)
+    ref.swiglu_ffn(dg, du, r)
+    assert_bits_equal(to_host(ops.swiglu_ffn(dg, du)), to_host(r), "vs reference")
+    assert ulp_error(oracle.swiglu_ffn(g, u), to_host(r)).max() <= ULP_TOL
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 4), (64, 2048), (48, 1536), (5, 200), (3, 6144)])
+def test_rms_norm_matches_reference(ref, oracle, rng, cuda, rows, hidden):
+    x = normal_bf16(rng, (rows, hidden), 1.5)
+    dx = to_dev(x, cuda)
+    r = torch.empty_like(dx)
+    ref.rms_norm(dx, r, 1e-6)
+    assert_bits_equal(to_host(ops.rms_norm(dx, eps=1e-6)), to_host(r), "vs reference")
+    assert_bits_equal(oracle.rms_norm(x, None, eps=1e-6), to_host(r), "oracle vs reference")
+
+
+def test_add_rms_norm_matches_reference_pair(ref, rng, cuda):
+    """Fused add+norm == the reference's additive_inject -> rms_norm sequence."""
+    x, b = to_dev(normal_bf16(rng, (256, 2048)), cuda), to_dev(normal_bf16(rng, (256, 2048)), cuda)
+    r_ref, y_ref = torch.empty_like(x), torch.empty_like(x)
+    ref.additive_inject(x, b, r_ref)
+    ref.rms_norm(r_ref, y_ref, 1e-6)
+    r, y = ops.add_rms_norm(x, b, eps=1e-6)
+    assert_bits_equal(to_host(r), to_host(r_ref), "residual")
+    assert_bits_equal(to_host(y), to_host(y_ref), "normed")
+
+
+def test_embedding_matches_reference(ref, oracle, rng, cuda):
+    table = normal_bf16(rng, (32000, 2048), 0.02)
+    ids = rng.integers(0, 32000, 4096, dtype=np.uint32)
+    ids[:2] = [32000, 0xFFFFFFFF]
+    dt, di = to_dev(table, cuda), to_dev(ids, cuda)
+    r = torch.empty((4096, 2048), dtype=torch.bfloat16, device=cuda)
+    ref.embedding_lookup(di, dt, r, 45.254834)
+    assert_bits_equal(to_host(ops.embedding_lookup(di, dt, 45.254834)), to_host(r), "vs reference")
+    assert_bits_equal(oracle.embedding_lookup(ids, table, 45.254834), to_host(r), "oracle vs reference")
+
+
+@pytest.mark.parametrize("b,h,s,d,off", [(2, 16, 512, 128, 0), (8, 16, 1, 128, 4095), (1, 4, 300, 64, 9)])
+@pytest.mark.parametrize("use_table", [False, True])
+def test_rope_matches_reference(ref, oracle, rng, cuda, b, h, s, d, off, use_table):
+    q, k = normal_bf16(rng, (b, h, s, d)), normal_bf16(rng, (b, h, s, d))
+    rq, rk = to_dev(q, cuda), to_dev(k, cuda)
+    ref.rope_embed(rq, rk, off, 10000.0)
+    mq, mk = to_dev(q, cuda), to_dev(k, cuda)
+    ops.rope_embed(mq, mk, off, 10000.0, ops.rope_table(off + s, d) if use_table else None)
+    assert_bits_equal(to_host(mq), to_host(rq), "q vs reference")
+    assert_bits_equal(to_host(mk), to_host(rk), "k vs reference")
+    oq, ok = oracle.rope_embed(q, k, off, 10000.0)
+    for got, want in ((oq, to_host(rq)), (ok, to_host(rk))):
+        assert ulp_error(got, want, rope_pair_magnitude(want)).max() <= ULP_TOL
