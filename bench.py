@@ -62,6 +62,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="chain",
                     choices=["chain", "add_rms_norm", "rms_norm_f32", "rope", "swiglu", "embedding"])
+    ap.add_argument("--tokens", type=int, default=CHAIN_B * CHAIN_S,
+                    help="chain tokens per GPU (a multiple of 4096; default 65536)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-oracle baseline leg")
     return ap.parse_args()
@@ -161,13 +163,16 @@ class Chain:
     name = "chain"
     dominant = "swiglu_ffn"
 
-    def __init__(self, device, rank):
+    def __init__(self, device, rank, tokens=CHAIN_B * CHAIN_S):
         import torch
 
         from hrm_layer_ops import chain, ops
 
+        if tokens % CHAIN_S or tokens <= 0:
+            raise SystemExit(f"--tokens must be a positive multiple of {CHAIN_S}")
         self.torch, self.chain, self.ops, self.device = torch, chain, ops, device
-        T = CHAIN_B * CHAIN_S
+        self.batch = tokens // CHAIN_S
+        T = tokens
         self.tokens = T
         wgen = torch.Generator(device=device).manual_seed(1234)          # weights: same on every rank
         gen = torch.Generator(device=device).manual_seed(1000 + rank)   # activations: this rank's shard
@@ -176,8 +181,8 @@ class Chain:
             w2=randn_bf16(HIDDEN, wgen, device, 0.1, 1.0), rope=ops.rope_table(CHAIN_S, HEAD_DIM, THETA, device),
             scale=SCALE, eps=EPS, theta=THETA)
         self.ids = torch.randint(0, VOCAB, (T,), generator=gen, device=device, dtype=torch.int32)
-        self.q = randn_bf16((CHAIN_B, HEADS, CHAIN_S, HEAD_DIM), gen, device)
-        self.k = randn_bf16((CHAIN_B, HEADS, CHAIN_S, HEAD_DIM), gen, device)
+        self.q = randn_bf16((self.batch, HEADS, CHAIN_S, HEAD_DIM), gen, device)
+        self.k = randn_bf16((self.batch, HEADS, CHAIN_S, HEAD_DIM), gen, device)
         self.o = randn_bf16((T, HIDDEN), gen, device)
         self.gate = randn_bf16((T, INTER), gen, device, 0.5)
         self.up = randn_bf16((T, INTER), gen, device, 0.5)
@@ -194,9 +199,9 @@ class Chain:
         self.footprint = per["op_sum"] * T
         self.config = {"workload": "chain: embed+RMSNorm -> RoPE -> add+RMSNorm -> SwiGLU",
                        "tokens_per_gpu": T, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM,
-                       "intermediate": INTER, "vocab": VOCAB, "qk_layout": [CHAIN_B, HEADS, CHAIN_S, HEAD_DIM],
+                       "intermediate": INTER, "vocab": VOCAB, "qk_layout": [self.batch, HEADS, CHAIN_S, HEAD_DIM],
                        "bytes_per_token_minimal": per["minimal"], "bytes_per_token_moved": per["op_sum"],
-                       "l2": "inputs larger than L2 (4.6 GB moved per step vs 126 MB L2); no flush"}
+                       "l2": f"inputs larger than L2 ({per['op_sum'] * T / 1e9:.1f} GB moved per step vs 126 MB L2); no flush"}
 
     def step(self, stream=None, events=None):
         self.chain.run_device(self.w, self.ids, self.q, self.k, self.o, self.gate, self.up, self.h, self.n1,
@@ -235,7 +240,7 @@ class Chain:
     # -- end to end: pinned host buffers through the public API
     def e2e(self, steps):
         torch = self.torch
-        hc = self.chain.HostChain(self.w, CHAIN_B, HEADS, CHAIN_S, HEAD_DIM, HIDDEN, INTER, chunk_batches=1,
+        hc = self.chain.HostChain(self.w, self.batch, HEADS, CHAIN_S, HEAD_DIM, HIDDEN, INTER, chunk_batches=1,
                                   device=self.device)
         pin = dict(pin_memory=True)
         host_in = {n: torch.empty(getattr(self, n).shape, dtype=getattr(self, n).dtype, **pin)
@@ -477,7 +482,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
-    wl = Chain(device, rank) if args.workload == "chain" else SingleOp(args.workload, device, rank)
+    wl = Chain(device, rank, args.tokens) if args.workload == "chain" else SingleOp(args.workload, device, rank)
     stream = torch.cuda.current_stream(device)
 
     for _ in range(args.warmup):

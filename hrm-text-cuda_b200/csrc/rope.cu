@@ -17,8 +17,12 @@
 // table, evaluated in the thread with exactly the reference expression
 //   (float)(s + offset) * expf(-2.0f * i * logf(theta) / (float)head_dim)
 // and sincosf (src/kernels/rope_embed.cu:41-43).  The table is built with that
-// same expression, so both ways give the reference's cos/sin bit for bit, and
-// the rotation uses the reference's expression (x0*c - x1*s, x1*c + x0*s).
+// same expression, so both ways give the reference's cos/sin bit for bit.
+// The rotation is written with explicit roundings in the form nvcc gives the
+// reference's `x0 * c - x1 * s` and `x1 * c + x0 * s`
+// (src/kernels/rope_embed.cu:47-53): fma(x0, c, -(x1 * s)) and
+// fma(x1, c, x0 * s).  Left to contraction, the same source expressions
+// compile differently here and round differently in ~2e-5 of the outputs.
 #include "common.cuh"
 #include "launch.h"
 
@@ -47,6 +51,14 @@ __device__ __forceinline__ float rope_angle(int pos, int i, int head_dim, float 
   return (float)pos * expf(-2.0f * i * logf(theta) / (float)head_dim);
 }
 
+// x0' and x1' of one pair, rounded as the reference kernel rounds them.
+__device__ __forceinline__ float rot_lo(float x0, float x1, float c, float s) {
+  return __fmaf_rn(x0, c, -__fmul_rn(x1, s));
+}
+__device__ __forceinline__ float rot_hi(float x0, float x1, float c, float s) {
+  return __fmaf_rn(x1, c, __fmul_rn(x0, s));
+}
+
 __device__ __forceinline__ void rotate8(uint4& lo, uint4& hi, const float (&c)[8], const float (&s)[8]) {
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
@@ -54,8 +66,8 @@ __device__ __forceinline__ void rotate8(uint4& lo, uint4& hi, const float (&c)[8
     const float x0a = bf16_lo(wl), x0b = bf16_hi(wl);
     const float x1a = bf16_lo(wh), x1b = bf16_hi(wh);
     const float ca = c[2 * w], sa = s[2 * w], cb = c[2 * w + 1], sb = s[2 * w + 1];
-    vset(lo, w, pack_bf16x2(x0a * ca - x1a * sa, x0b * cb - x1b * sb));
-    vset(hi, w, pack_bf16x2(x1a * ca + x0a * sa, x1b * cb + x0b * sb));
+    vset(lo, w, pack_bf16x2(rot_lo(x0a, x1a, ca, sa), rot_lo(x0b, x1b, cb, sb)));
+    vset(hi, w, pack_bf16x2(rot_hi(x0a, x1a, ca, sa), rot_hi(x0b, x1b, cb, sb)));
   }
 }
 
@@ -145,11 +157,11 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(uint16_t* q, uint16_t*
     }
     const int64_t i0 = row * head_dim + i, i1 = i0 + half;
     const float x0 = bf16_to_f32(q[i0]), x1 = bf16_to_f32(q[i1]);
-    q[i0] = f32_to_bf16(x0 * c - x1 * s);
-    q[i1] = f32_to_bf16(x1 * c + x0 * s);
+    q[i0] = f32_to_bf16(rot_lo(x0, x1, c, s));
+    q[i1] = f32_to_bf16(rot_hi(x0, x1, c, s));
     const float k0 = bf16_to_f32(k[i0]), k1 = bf16_to_f32(k[i1]);
-    k[i0] = f32_to_bf16(k0 * c - k1 * s);
-    k[i1] = f32_to_bf16(k1 * c + k0 * s);
+    k[i0] = f32_to_bf16(rot_lo(k0, k1, c, s));
+    k[i1] = f32_to_bf16(rot_hi(k0, k1, c, s));
   }
 }
 

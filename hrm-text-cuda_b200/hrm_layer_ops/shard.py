@@ -1,0 +1,84 @@
+"""Row sharding across GPUs (one process per GPU, torch.distributed).
+
+Token rows are independent in every layer op (the norms reduce within a row
+only), so a job splits into contiguous row ranges with no data exchange:
+
+* row ops ([rows, hidden]):  rows [r0, r1) per rank, balanced to within one row;
+* RoPE ([batch, heads, seq, head_dim]): along batch when there are at least as
+  many batches as ranks, otherwise along seq, where a rank's slice starting at
+  s0 is rotated with position_offset + s0 -- the reference's own
+  position_offset parameter (src/lib.rs:821-827) makes a mid-sequence shard
+  exact.
+
+The collectives here are for timing and verification only: the maximum of
+per-rank times, and gathering shards (or their checksums) to compare against
+an unsharded run.  They work on any backend (gloo on CPU tensors, NCCL on
+CUDA tensors).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def row_range(total_rows: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous [start, stop) of `total_rows` for `rank`; sizes differ by <= 1."""
+    if world <= 0 or not 0 <= rank < world or total_rows < 0:
+        raise ValueError("bad shard arguments")
+    base, extra = divmod(total_rows, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+@dataclass(frozen=True)
+class RopeShard:
+    b0: int
+    b1: int
+    s0: int
+    s1: int
+    position_offset: int  # offset to pass to rope_embed for this shard
+
+
+def rope_shard(batch: int, seq: int, position_offset: int, world: int, rank: int) -> RopeShard:
+    """Shard of a [batch, heads, seq, head_dim] RoPE call for `rank`."""
+    if batch >= world:
+        b0, b1 = row_range(batch, world, rank)
+        return RopeShard(b0, b1, 0, seq, position_offset)
+    s0, s1 = row_range(seq, world, rank)
+    return RopeShard(0, batch, s0, s1, position_offset + s0)
+
+
+def max_over_ranks(value: float, device=None) -> float:
+    """Maximum of a per-rank scalar (e.g. a CUDA-event time) over all ranks."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gather_rows(shard: torch.Tensor, total_rows: int) -> torch.Tensor:
+    """All-gathers row shards (as split by row_range) into the full tensor on every rank."""
+    world, rank = dist.get_world_size(), dist.get_rank()
+    counts = [row_range(total_rows, world, r)[1] - row_range(total_rows, world, r)[0] for r in range(world)]
+    if shard.shape[0] != counts[rank]:
+        raise ValueError("shard does not match row_range")
+    # move raw bytes: every backend can all_gather uint8 (gloo has no 16-bit ints)
+    raw = shard.contiguous().reshape(shard.shape[0], -1).view(torch.uint8)
+    pad = torch.zeros((max(counts), raw.shape[1]), dtype=torch.uint8, device=shard.device)
+    pad[: raw.shape[0]] = raw
+    parts: List[torch.Tensor] = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad)
+    full = torch.cat([p[:c] for p, c in zip(parts, counts)], dim=0)
+    return full.view(shard.dtype).reshape(total_rows, *shard.shape[1:])
+
+
+def checksum(t: torch.Tensor) -> int:
+    """Order-sensitive 64-bit checksum of a tensor's bytes (same on CPU and GPU)."""
+    b = t.contiguous().view(torch.int16 if t.element_size() == 2 else torch.int32).reshape(-1).to(torch.int64)
+    idx = torch.arange(b.numel(), device=b.device, dtype=torch.int64)
+    return int(((b & 0xFFFF if t.element_size() == 2 else b) * (idx % 65521 + 1)).sum().item())

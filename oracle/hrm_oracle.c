@@ -186,6 +186,11 @@ void ora_rope_table(float* table, int64_t positions, int64_t head_dim, float the
     }
 }
 
+/* rope_embed.cu:45-53 as nvcc contracts it: x0' = fma(x0, c, -(x1 * s)),
+ * x1' = fma(x1, c, x0 * s) (established by running the reference kernel). */
+static float rot_lo(float x0, float x1, float c, float s) { return fmaf(x0, c, -(x1 * s)); }
+static float rot_hi(float x0, float x1, float c, float s) { return fmaf(x1, c, x0 * s); }
+
 /* rope_embed.cu:27-53: pair (i, i + D/2) of row (b, h, s), Q then K. */
 void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                     int64_t offset, float theta, const float* table) {
@@ -205,11 +210,11 @@ void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int6
       }
       const int64_t i0 = row * head_dim + i, i1 = i0 + half;
       const float x0 = ora_bf16_to_f32(q[i0]), x1 = ora_bf16_to_f32(q[i1]);
-      q[i0] = ora_f32_to_bf16(x0 * c - x1 * s);
-      q[i1] = ora_f32_to_bf16(x1 * c + x0 * s);
+      q[i0] = ora_f32_to_bf16(rot_lo(x0, x1, c, s));
+      q[i1] = ora_f32_to_bf16(rot_hi(x0, x1, c, s));
       const float k0 = ora_bf16_to_f32(k[i0]), k1 = ora_bf16_to_f32(k[i1]);
-      k[i0] = ora_f32_to_bf16(k0 * c - k1 * s);
-      k[i1] = ora_f32_to_bf16(k1 * c + k0 * s);
+      k[i0] = ora_f32_to_bf16(rot_lo(k0, k1, c, s));
+      k[i1] = ora_f32_to_bf16(rot_hi(k0, k1, c, s));
     }
   }
 }

@@ -11,8 +11,8 @@
  *
  * bf16 values are uint16_t bit patterns.  Arithmetic is IEEE fp32 with no
  * contraction (built with -ffp-contract=off); where the reference's nvcc
- * build contracts a multiply-add into an FMA that changes the result (the
- * RMSNorm sum of squares) the oracle calls fmaf explicitly.  Transcendentals
+ * build contracts a multiply-add into an FMA (the RMSNorm sum of squares, the
+ * RoPE rotation) the oracle calls fmaf in the same place.  Transcendentals
  * come from the C library (expf, logf, sinf, cosf), not CUDA's; the tests
  * allow for that difference (2 bf16 ulp) where it can show.
  */

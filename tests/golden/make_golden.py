@@ -44,13 +44,13 @@ KATS = {
 # Seeded cases run through the reference kernels (small enough for the CPU
 # oracle in well under a second each).
 REF_CASES = {
-    "rms_norm": dict(rows=64, hidden=2048, eps=1e-5),
+    "rms_norm": dict(rows=32, hidden=2048, eps=1e-5),
     "rms_norm_h1536": dict(rows=48, hidden=1536, eps=1e-6),
     "rms_norm_h200": dict(rows=8, hidden=200, eps=1e-6),
-    "additive_inject": dict(n=65536 + 5),
-    "swiglu_ffn": dict(n=262144 + 3),
-    "embedding_lookup": dict(vocab=1000, hidden=2048, tokens=257, scale=45.254834),
-    "rope_embed": dict(batch=2, heads=4, seq=300, head_dim=128, offset=0, theta=10000.0),
+    "additive_inject": dict(n=16384 + 5),
+    "swiglu_ffn": dict(n=65536 + 3),
+    "embedding_lookup": dict(vocab=300, hidden=2048, tokens=130, scale=45.254834),
+    "rope_embed": dict(batch=1, heads=4, seq=160, head_dim=128, offset=0, theta=10000.0),
     "rope_embed_decode": dict(batch=4, heads=16, seq=1, head_dim=128, offset=4095, theta=10000.0),
     "rope_embed_hd64": dict(batch=1, heads=2, seq=77, head_dim=64, offset=3, theta=500000.0),
 }

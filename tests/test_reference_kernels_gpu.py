@@ -11,6 +11,8 @@ the same reference outputs (bit-exact / <= 2 bf16 ulp), which is what pins
 the oracle to the reference.
 """
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -93,3 +95,76 @@ def test_rope_matches_reference(ref, oracle, rng, cuda, b, h, s, d, off, use_tab
     oq, ok = oracle.rope_embed(q, k, off, 10000.0)
     for got, want in ((oq, to_host(rq)), (ok, to_host(rk))):
         assert ulp_error(got, want, rope_pair_magnitude(want)).max() <= ULP_TOL
+
+
+# ------------------------------------------------ speed vs the reference
+def _time(fn, iters=20, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(iters):
+        fn()
+    t1.record()
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / iters
+
+
+def test_throughput_vs_reference_kernels(ref, cuda):
+    """Both implementations at the full layer-op configurations, same inputs, same
+    GPU, CUDA events (inputs > L2 except the 67 MB norm, which rotates 8 copies).
+    Prints a JSON line (GB/s of algorithmic bytes) and requires this library to be
+    at least as fast as the reference kernels on every op."""
+    import json
+
+    g = torch.Generator(device=cuda).manual_seed(0)
+    bf = torch.bfloat16
+
+    def rn(shape, std=1.0):
+        return (torch.randn(shape, generator=g, device=cuda) * std).to(bf)
+
+    res = {}
+    # fused add + RMSNorm [16384 x 2048] vs additive_inject -> rms_norm (no weight: the reference has none)
+    x, b = rn((16384, 2048)), rn((16384, 2048))
+    r, y = torch.empty_like(x), torch.empty_like(x)
+    nbytes = 16384 * 2048 * 2 * 4
+    res["add_rms_norm"] = (nbytes / _time(lambda: ops.add_rms_norm(x, b, None, 1e-5, residual_out=r, normed_out=y)),
+                           nbytes / _time(lambda: (ref.additive_inject(x, b, r), ref.rms_norm(r, y, 1e-5))))
+    # RMSNorm bf16 [4096 x 2048] (8 rotating copies: 268 MB > L2)
+    xs = [rn((4096, 2048)) for _ in range(8)]
+    ys = [torch.empty_like(xs[0]) for _ in range(8)]
+    it = iter(range(10 ** 9))
+    nb = 4096 * 2048 * 2 * 2
+    res["rms_norm"] = (nb / _time(lambda: (lambda i: ops.rms_norm(xs[i % 8], None, 1e-5, out=ys[i % 8]))(next(it))),
+                       nb / _time(lambda: (lambda i: ref.rms_norm(xs[i % 8], ys[i % 8], 1e-5))(next(it))))
+    # RoPE Q/K [8, 16, 4096, 128]: table path and in-kernel angles vs the reference
+    q, k = rn((8, 16, 4096, 128)), rn((8, 16, 4096, 128))
+    table = ops.rope_table(4096, 128)
+    nb = q.numel() * 2 * 4
+    t_ref = _time(lambda: ref.rope_embed(q, k, 0, 10000.0))
+    res["rope_table"] = (nb / _time(lambda: ops.rope_embed(q, k, 0, 10000.0, table)), nb / t_ref)
+    res["rope_in_kernel"] = (nb / _time(lambda: ops.rope_embed(q, k, 0, 10000.0, None)), nb / t_ref)
+    del q, k
+    # SwiGLU [32768 x 5632]
+    gg, uu = rn((32768, 5632), 0.5), rn((32768, 5632), 0.5)
+    oo = torch.empty_like(gg)
+    nb = gg.numel() * 6
+    res["swiglu"] = (nb / _time(lambda: ops.swiglu_ffn(gg, uu, out=oo)), nb / _time(lambda: ref.swiglu_ffn(gg, uu, oo)))
+    del gg, uu, oo
+    # embedding [32000 x 2048], 65536 ids
+    tab = rn((32000, 2048), 0.02)
+    ids = torch.randint(0, 32000, (65536,), generator=g, device=cuda, dtype=torch.int32)
+    eo = torch.empty((65536, 2048), dtype=bf, device=cuda)
+    nb = 65536 * (4 + 2 * 2 * 2048)
+    res["embedding"] = (nb / _time(lambda: ops.embedding_lookup(ids, tab, 45.254834, out=eo)),
+                        nb / _time(lambda: ref.embedding_lookup(ids, tab, eo, 45.254834)))
+    out = {k: {"ours_gbs": round(a / 1e6, 1), "reference_gbs": round(b_ / 1e6, 1), "speedup": round(a / b_, 2)}
+           for k, (a, b_) in res.items()}
+    print(json.dumps({"vs_reference_kernels": out}))
+    path = os.environ.get("HRM_REF_TIMING_OUT")
+    if path:
+        with open(path, "w") as f:
+            json.dump(out, f, indent=1)
+    for k, v in out.items():
+        assert v["speedup"] >= 0.95, (k, v)
