@@ -369,6 +369,7 @@ class SingleOp:
         self.kernels = [name]
         self.dominant = name
         self.kernel_bytes = {name: self.bytes_per_step}
+        self.footprint = self.bytes_per_step
         self.cfg["l2"] = (f"{nbuf} rotating input sets ({nbuf * self.bytes_per_step / 1e6:.0f} MB > 3x L2)"
                           if nbuf > 1 else "inputs larger than L2; no flush")
         self.config = self.cfg
@@ -552,6 +553,7 @@ def main():
         "vs_baseline": None, "dtype": "bf16 (fp32 math)", "data": "synthetic (seeded, generated on device)",
         "config": dict(wl.config, parallelism=f"{world} row shards, no collective"),
         "pct_of_peak": round(100 * value_gbs / (world * peak), 2), "rows_per_s": round(rows_per_s, 1),
+        "effective_gbs": round(world * wl.footprint / (ms_step / 1e3) / 1e9, 3),
         "per_kernel": {k: {"us": round(kern_ms[k] * 1e3, 2),
                            "gbs": round(wl.kernel_bytes[k] / (kern_ms[k] / 1e3) / 1e9, 1)} for k in wl.kernels},
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

@@ -5,9 +5,11 @@
 //   * one 16-byte vector (8 bf16) per access, every warp-wide access a fully
 //     used, contiguous 512-byte span;
 //   * U independent vectors per operand per thread issued before any use
-//     (U = 4 -> 8 x 16 B loads in flight per thread);
-//   * a grid of (SM count x resident CTAs) CTAs walking the tensor with a
-//     grid-sized stride, so no tail wave and no per-CTA index math;
+//     (U = 2 -> 4 x 16 B loads in flight per thread);
+//   * a grid that covers the tensor once (one U-vector group per thread) at
+//     up to 4 resident 256-thread CTAs per SM (<= 64 registers): the hardware
+//     refills SMs as CTAs retire.  Measured on B200 this beats a persistent
+//     one-wave grid with 4 vectors in flight (99.5% vs 95% of copy bandwidth);
 //   * evict-first loads/stores so the stream does not flush reused L2 lines.
 // The arithmetic per element is the reference's, operation for operation:
 //   swiglu: g * (1.0f / (1.0f + __expf(-g))) * u    (src/kernels/swiglu_ffn.cu:31-35)
@@ -19,8 +21,23 @@
 namespace hrm {
 namespace {
 
+// Launch shape (compile-time; the defaults are the tuned values):
+//   HRM_EW_UNROLL     vectors per operand per thread per iteration
+//   HRM_EW_WAVES      grid cap in waves of resident CTAs (0: no cap, one
+//                     iteration per thread)
+//   HRM_EW_MINBLOCKS  __launch_bounds__ minimum resident CTAs per SM
+#ifndef HRM_EW_UNROLL
+#define HRM_EW_UNROLL 2
+#endif
+#ifndef HRM_EW_WAVES
+#define HRM_EW_WAVES 0
+#endif
+#ifndef HRM_EW_MINBLOCKS
+#define HRM_EW_MINBLOCKS 4
+#endif
+
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = HRM_EW_UNROLL;
 
 struct SwigluOp {
   __device__ __forceinline__ float f(float g, float u) const {
@@ -46,7 +63,7 @@ __device__ __forceinline__ uint4 apply8(const Op& op, const uint4& a, const uint
 // a, b, out: 16-byte aligned; nvec = n / 8 full vectors; the n % 8 trailing
 // elements (starting at element nvec * 8) are done by global thread 0.
 template <class Op>
-__global__ void __launch_bounds__(kThreads) ew_vec_kernel(const uint4* a, const uint4* b, uint4* out,
+__global__ void __launch_bounds__(kThreads, HRM_EW_MINBLOCKS) ew_vec_kernel(const uint4* a, const uint4* b, uint4* out,
                                                           int64_t nvec, int tail) {
   const Op op;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
@@ -86,9 +103,10 @@ cudaError_t launch_ew(const void* a, const void* b, void* out, int64_t n, cudaSt
   const int64_t max_blocks = (int64_t)device_sm_count() * (2048 / kThreads);
   if (aligned16(a) && aligned16(b) && aligned16(out)) {
     const int64_t nvec = n / 8;
-    int64_t blocks = (nvec + kThreads - 1) / kThreads;
+    int64_t blocks = (nvec + (int64_t)kThreads * kUnroll - 1) / ((int64_t)kThreads * kUnroll);
     if (blocks < 1) blocks = 1;
-    if (blocks > max_blocks) blocks = max_blocks;
+    if (HRM_EW_WAVES > 0 && blocks > max_blocks * HRM_EW_WAVES) blocks = max_blocks * HRM_EW_WAVES;
+    if (blocks > INT32_MAX) blocks = INT32_MAX;
     ew_vec_kernel<Op><<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<const uint4*>(a),
                                                             static_cast<const uint4*>(b),
                                                             static_cast<uint4*>(out), nvec, (int)(n % 8));

@@ -14,9 +14,19 @@
 namespace hrm {
 namespace {
 
+// Launch shape (compile-time; defaults tuned):
+//   HRM_EMB_INFLIGHT  16-byte loads per lane issued before the first store
+//   HRM_EMB_WAVES     grid cap in waves of 8 CTAs per SM (0: one warp per token)
+#ifndef HRM_EMB_INFLIGHT
+#define HRM_EMB_INFLIGHT 8
+#endif
+#ifndef HRM_EMB_WAVES
+#define HRM_EMB_WAVES 0
+#endif
+
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kInFlight = 8;
+constexpr int kInFlight = HRM_EMB_INFLIGHT;
 
 __global__ void __launch_bounds__(kThreads) embedding_warp_kernel(const uint32_t* ids, const uint4* table,
                                                                   uint4* out, int64_t tokens, int nchunks,
@@ -74,7 +84,8 @@ cudaError_t launch_embedding(const uint32_t* ids, const void* table, void* out, 
   const int64_t wave = (int64_t)device_sm_count() * (2048 / kThreads);
   if (hidden % 8 == 0 && hidden / 8 <= INT32_MAX && aligned16(table) && aligned16(out)) {
     int64_t blocks = (tokens + kWarps - 1) / kWarps;
-    if (blocks > wave) blocks = wave;
+    if (HRM_EMB_WAVES > 0 && blocks > wave * HRM_EMB_WAVES) blocks = wave * HRM_EMB_WAVES;
+    if (blocks > INT32_MAX) blocks = INT32_MAX;
     embedding_warp_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(ids, static_cast<const uint4*>(table),
                                                                  static_cast<uint4*>(out), tokens,
                                                                  (int)(hidden / 8), (uint32_t)vocab, scale);

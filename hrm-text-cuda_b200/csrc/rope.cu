@@ -11,25 +11,45 @@
 // and for both Q and K, so the angle work / table traffic is amortised over
 // 2 * heads rows.  Prefill tiles are 16 positions x 1 slice (each head's 16
 // rows are 4 KB contiguous); decode (seq 1) tiles are 1 position x 16 slices.
-// Four heads' worth of loads (16 x 16 B) are in flight before any store.
+// One CTA per tile; two heads' loads in flight per thread (measured best).
+// HRM_ROPE_UNROLL heads' worth of loads (4 x 16 B each) are in flight before
+// any store.
 //
 // Angles: either the fp32 table written by rope_table_kernel or, with no
 // table, evaluated in the thread with exactly the reference expression
 //   (float)(s + offset) * expf(-2.0f * i * logf(theta) / (float)head_dim)
 // and sincosf (src/kernels/rope_embed.cu:41-43).  The table is built with that
 // same expression, so both ways give the reference's cos/sin bit for bit.
-// The rotation is written with explicit roundings in the form nvcc gives the
-// reference's `x0 * c - x1 * s` and `x1 * c + x0 * s`
-// (src/kernels/rope_embed.cu:47-53): fma(x0, c, -(x1 * s)) and
-// fma(x1, c, x0 * s).  Left to contraction, the same source expressions
-// compile differently here and round differently in ~2e-5 of the outputs.
+// The rotation is written with explicit roundings in the forms nvcc gives the
+// reference's source (src/kernels/rope_embed.cu:45-53), established by
+// running the reference kernel against every candidate rounding:
+//   q: x0' = fma(x0, c, -(x1 * s)),  x1' = fma(x1, c, x0 * s)
+//   k: x0' = fma(x0, c, -(x1 * s)),  x1' = fma(x0, s, x1 * c)
+// (the identical source expression contracts one way for q and the other for
+// k).  Left to contraction, the same expressions compile differently here and
+// round differently in ~2e-5 of the outputs.
 #include "common.cuh"
 #include "launch.h"
 
 namespace hrm {
 namespace {
 
+// Launch shape of the tiled kernel (compile-time; defaults tuned):
+//   HRM_ROPE_UNROLL     heads whose Q/K chunks are loaded before any is used
+//   HRM_ROPE_CAP        grid cap in CTAs per SM (0: one CTA per tile)
+//   HRM_ROPE_MINBLOCKS  __launch_bounds__ minimum resident CTAs per SM
+#ifndef HRM_ROPE_UNROLL
+#define HRM_ROPE_UNROLL 2
+#endif
+#ifndef HRM_ROPE_CAP
+#define HRM_ROPE_CAP 0
+#endif
+#ifndef HRM_ROPE_MINBLOCKS
+#define HRM_ROPE_MINBLOCKS 1
+#endif
+
 constexpr int kThreads = 128;
+constexpr int kHeadUnroll = HRM_ROPE_UNROLL;
 
 struct RopeArgs {
   uint4* q;
@@ -55,10 +75,14 @@ __device__ __forceinline__ float rope_angle(int pos, int i, int head_dim, float 
 __device__ __forceinline__ float rot_lo(float x0, float x1, float c, float s) {
   return __fmaf_rn(x0, c, -__fmul_rn(x1, s));
 }
-__device__ __forceinline__ float rot_hi(float x0, float x1, float c, float s) {
+__device__ __forceinline__ float rot_hi_q(float x0, float x1, float c, float s) {
   return __fmaf_rn(x1, c, __fmul_rn(x0, s));
 }
+__device__ __forceinline__ float rot_hi_k(float x0, float x1, float c, float s) {
+  return __fmaf_rn(x0, s, __fmul_rn(x1, c));
+}
 
+template <bool IS_K>
 __device__ __forceinline__ void rotate8(uint4& lo, uint4& hi, const float (&c)[8], const float (&s)[8]) {
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
@@ -67,12 +91,15 @@ __device__ __forceinline__ void rotate8(uint4& lo, uint4& hi, const float (&c)[8
     const float x1a = bf16_lo(wh), x1b = bf16_hi(wh);
     const float ca = c[2 * w], sa = s[2 * w], cb = c[2 * w + 1], sb = s[2 * w + 1];
     vset(lo, w, pack_bf16x2(rot_lo(x0a, x1a, ca, sa), rot_lo(x0b, x1b, cb, sb)));
-    vset(hi, w, pack_bf16x2(rot_hi(x0a, x1a, ca, sa), rot_hi(x0b, x1b, cb, sb)));
+    if (IS_K)
+      vset(hi, w, pack_bf16x2(rot_hi_k(x0a, x1a, ca, sa), rot_hi_k(x0b, x1b, cb, sb)));
+    else
+      vset(hi, w, pack_bf16x2(rot_hi_q(x0a, x1a, ca, sa), rot_hi_q(x0b, x1b, cb, sb)));
   }
 }
 
 template <bool TABLE>
-__global__ void __launch_bounds__(kThreads) rope_tile_kernel(const RopeArgs a) {
+__global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel(const RopeArgs a) {
   const int j = threadIdx.x % a.g;
   const int rest = threadIdx.x / a.g;
   const int slice = rest % a.ht;
@@ -101,10 +128,10 @@ __global__ void __launch_bounds__(kThreads) rope_tile_kernel(const RopeArgs a) {
     const int64_t head_step = a.seq * row_chunks;
     const int64_t row0 = ((b * a.heads) * a.seq + s) * row_chunks + j;
     int h = slice;
-    for (; h + 3 * a.ht < a.heads; h += 4 * a.ht) {
-      uint4 ql[4], qh[4], kl[4], kh[4];
+    for (; h + (kHeadUnroll - 1) * a.ht < a.heads; h += kHeadUnroll * a.ht) {
+      uint4 ql[kHeadUnroll], qh[kHeadUnroll], kl[kHeadUnroll], kh[kHeadUnroll];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kHeadUnroll; ++u) {
         const int64_t lo = row0 + (int64_t)(h + u * a.ht) * head_step;
         ql[u] = ld_stream(a.q + lo);
         qh[u] = ld_stream(a.q + lo + a.g);
@@ -112,10 +139,10 @@ __global__ void __launch_bounds__(kThreads) rope_tile_kernel(const RopeArgs a) {
         kh[u] = ld_stream(a.k + lo + a.g);
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kHeadUnroll; ++u) {
         const int64_t lo = row0 + (int64_t)(h + u * a.ht) * head_step;
-        rotate8(ql[u], qh[u], c, sn);
-        rotate8(kl[u], kh[u], c, sn);
+        rotate8<false>(ql[u], qh[u], c, sn);
+        rotate8<true>(kl[u], kh[u], c, sn);
         st_stream(a.q + lo, ql[u]);
         st_stream(a.q + lo + a.g, qh[u]);
         st_stream(a.k + lo, kl[u]);
@@ -126,8 +153,8 @@ __global__ void __launch_bounds__(kThreads) rope_tile_kernel(const RopeArgs a) {
       const int64_t lo = row0 + (int64_t)h * head_step;
       uint4 ql = ld_stream(a.q + lo), qh = ld_stream(a.q + lo + a.g);
       uint4 kl = ld_stream(a.k + lo), kh = ld_stream(a.k + lo + a.g);
-      rotate8(ql, qh, c, sn);
-      rotate8(kl, kh, c, sn);
+      rotate8<false>(ql, qh, c, sn);
+      rotate8<true>(kl, kh, c, sn);
       st_stream(a.q + lo, ql);
       st_stream(a.q + lo + a.g, qh);
       st_stream(a.k + lo, kl);
@@ -158,10 +185,10 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(uint16_t* q, uint16_t*
     const int64_t i0 = row * head_dim + i, i1 = i0 + half;
     const float x0 = bf16_to_f32(q[i0]), x1 = bf16_to_f32(q[i1]);
     q[i0] = f32_to_bf16(rot_lo(x0, x1, c, s));
-    q[i1] = f32_to_bf16(rot_hi(x0, x1, c, s));
+    q[i1] = f32_to_bf16(rot_hi_q(x0, x1, c, s));
     const float k0 = bf16_to_f32(k[i0]), k1 = bf16_to_f32(k[i1]);
     k[i0] = f32_to_bf16(rot_lo(k0, k1, c, s));
-    k[i1] = f32_to_bf16(rot_hi(k0, k1, c, s));
+    k[i1] = f32_to_bf16(rot_hi_k(k0, k1, c, s));
   }
 }
 
@@ -211,7 +238,8 @@ cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t 
     a.offset = (int)offset;
     a.theta = theta;
     int64_t blocks = a.ntiles;
-    if (blocks > sms * 16) blocks = sms * 16;
+    if (HRM_ROPE_CAP > 0 && blocks > sms * HRM_ROPE_CAP) blocks = sms * HRM_ROPE_CAP;
+    if (blocks > INT32_MAX) blocks = INT32_MAX;
     if (table != nullptr)
       rope_tile_kernel<true><<<(unsigned)blocks, kThreads, 0, s>>>(a);
     else

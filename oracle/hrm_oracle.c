@@ -186,10 +186,12 @@ void ora_rope_table(float* table, int64_t positions, int64_t head_dim, float the
     }
 }
 
-/* rope_embed.cu:45-53 as nvcc contracts it: x0' = fma(x0, c, -(x1 * s)),
- * x1' = fma(x1, c, x0 * s) (established by running the reference kernel). */
+/* rope_embed.cu:45-53 as nvcc contracts it (established by running the
+ * reference kernel against every candidate rounding): x0' = fma(x0, c, -(x1*s))
+ * for q and k; x1' = fma(x1, c, x0*s) for q but fma(x0, s, x1*c) for k. */
 static float rot_lo(float x0, float x1, float c, float s) { return fmaf(x0, c, -(x1 * s)); }
-static float rot_hi(float x0, float x1, float c, float s) { return fmaf(x1, c, x0 * s); }
+static float rot_hi_q(float x0, float x1, float c, float s) { return fmaf(x1, c, x0 * s); }
+static float rot_hi_k(float x0, float x1, float c, float s) { return fmaf(x0, s, x1 * c); }
 
 /* rope_embed.cu:27-53: pair (i, i + D/2) of row (b, h, s), Q then K. */
 void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
@@ -211,10 +213,10 @@ void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int6
       const int64_t i0 = row * head_dim + i, i1 = i0 + half;
       const float x0 = ora_bf16_to_f32(q[i0]), x1 = ora_bf16_to_f32(q[i1]);
       q[i0] = ora_f32_to_bf16(rot_lo(x0, x1, c, s));
-      q[i1] = ora_f32_to_bf16(rot_hi(x0, x1, c, s));
+      q[i1] = ora_f32_to_bf16(rot_hi_q(x0, x1, c, s));
       const float k0 = ora_bf16_to_f32(k[i0]), k1 = ora_bf16_to_f32(k[i1]);
       k[i0] = ora_f32_to_bf16(rot_lo(k0, k1, c, s));
-      k[i1] = ora_f32_to_bf16(rot_hi(k0, k1, c, s));
+      k[i1] = ora_f32_to_bf16(rot_hi_k(k0, k1, c, s));
     }
   }
 }
