@@ -2,7 +2,7 @@
 """Throughput benchmark of the sm_100a per-token layer operators.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload chain|add_rms_norm|rms_norm_f32|rope|swiglu|embedding]
+                    [--workload chain|add_rms_norm|rms_norm_f32|rope|swiglu|embedding|split_rope]
 
 Default workload ("chain"): the chained layer-op pass on 65536 tokens per GPU
 -- embedding [32000 x 2048] ~ N(0, 0.02) gathered for ids ~ U[0, 32000) and
@@ -61,7 +61,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="chain",
-                    choices=["chain", "add_rms_norm", "rms_norm_f32", "rope", "swiglu", "embedding"])
+                    choices=["chain", "add_rms_norm", "rms_norm_f32", "rope", "swiglu", "embedding", "split_rope"])
     ap.add_argument("--tokens", type=int, default=CHAIN_B * CHAIN_S,
                     help="chain tokens per GPU (a multiple of 4096; default 65536)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
@@ -360,6 +360,16 @@ class SingleOp:
             mk = lambda: (torch.randint(0, VOCAB, (T,), generator=gen, device=device, dtype=torch.int32),
                           torch.empty((T, HIDDEN), dtype=bf, device=device))
             self.cfg = {"workload": "embedding gather [32000 x 2048] table, 65536 ids", "tokens": T}
+        elif name == "split_rope":        # gqkv [16, 4096, 4 x 16 x 128] -> gate, q, k, v + KV cache, table
+            B, S = 16, 4096
+            T = B * S
+            self.table = ops.rope_table(S, HEAD_DIM, THETA, device)
+            self.bytes_per_step, self.rows_per_step = T * (4 + 4 + 2) * HEADS * HEAD_DIM * 2, T
+            mk = lambda: (randn_bf16((B, S, 4 * HEADS * HEAD_DIM), gen, device),
+                          torch.empty((B, S, HEADS, HEAD_DIM), dtype=bf, device=device),
+                          *(torch.empty((B, HEADS, S, HEAD_DIM), dtype=bf, device=device) for _ in range(5)))
+            self.cfg = {"workload": "split_gqkv + RoPE + KV-cache write, gqkv [16, 4096, 4 x 16 x 128] bf16",
+                        "tokens": T}
         else:
             raise ValueError(name)
         # Rotate input sets so that their total exceeds 3x L2: no step finds its inputs in L2.
@@ -387,6 +397,8 @@ class SingleOp:
             ops.rope_embed(b[0], b[1], 0, THETA, self.table, stream=stream)
         elif self.name == "swiglu":
             ops.swiglu_ffn(b[0], b[1], out=b[2], stream=stream)
+        elif self.name == "split_rope":
+            ops.split_gqkv_rope(b[0], HEADS, 0, THETA, self.table, b[5], b[6], 0, out=b[1:5], stream=stream)
         else:
             ops.embedding_lookup(b[0], self.tab, SCALE, out=b[1], stream=stream)
         if events is not None:
@@ -397,7 +409,8 @@ class SingleOp:
         """Per step: H2D of the inputs from pinned host memory, the kernel, D2H of the outputs."""
         torch = self.torch
         b = self.bufs[0]
-        n_in = {"add_rms_norm": 2, "rms_norm_f32": 1, "rope": 2, "swiglu": 2, "embedding": 1}[self.name]
+        n_in = {"add_rms_norm": 2, "rms_norm_f32": 1, "rope": 2, "swiglu": 2, "embedding": 1,
+                "split_rope": 1}[self.name]
         outs = [0, 1] if self.name == "rope" else list(range(n_in, len(b)))
         host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in b]
         for h, t in zip(host, b):

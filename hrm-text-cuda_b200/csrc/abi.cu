@@ -199,4 +199,39 @@ int hrm_embed_rms_norm(const uint32_t* input_ids, const void* embedding_table, v
                                                 hidden_size, vocab_size, embedding_scale, eps, as_cuda(stream)));
 }
 
+int hrm_split_gqkv_rope(const void* gqkv, void* gate_out, void* q_out, void* k_out, void* v_out, void* k_cache,
+                        void* v_cache, int64_t batch_size, int64_t seq_len, int64_t num_heads, int64_t head_dim,
+                        int64_t position_offset, float theta, const float* rope_table, int64_t table_positions,
+                        int64_t cache_len, int64_t cache_offset, hrm_stream_t stream) {
+  if (batch_size < 0 || num_heads < 0 || seq_len < 0 || head_dim <= 0 || head_dim % 2 != 0 ||
+      position_offset < 0 || cache_offset < 0 || num_heads > INT32_MAX || head_dim > INT32_MAX)
+    return HRM_ERR_INVALID_SHAPE;
+  if (position_offset + seq_len > INT32_MAX) return HRM_ERR_SIZE_OVERFLOW;
+  if ((k_cache == nullptr) != (v_cache == nullptr)) return HRM_ERR_NULL_POINTER;
+  const bool cache = k_cache != nullptr;
+  if (cache && (cache_len < 0 || cache_offset + seq_len > cache_len)) return HRM_ERR_INVALID_SHAPE;
+  if (batch_size == 0 || num_heads == 0 || seq_len == 0) return HRM_OK;
+  if (!gqkv || !gate_out || !q_out || !k_out || !v_out) return HRM_ERR_NULL_POINTER;
+  const int64_t bytes = mul_checked(mul_checked(mul_checked(mul_checked(batch_size, num_heads), seq_len), head_dim), 2);
+  const int64_t in_bytes = mul_checked(bytes, 4);
+  const int64_t cbytes =
+      cache ? mul_checked(mul_checked(mul_checked(mul_checked(batch_size, num_heads), cache_len), head_dim), 2) : 0;
+  if (bytes < 0 || in_bytes < 0 || cbytes < 0) return HRM_ERR_SIZE_OVERFLOW;
+  const void* bufs[7] = {gqkv, gate_out, q_out, k_out, v_out, k_cache, v_cache};
+  const int64_t sizes[7] = {in_bytes, bytes, bytes, bytes, bytes, cbytes, cbytes};
+  for (int x = 0; x < 7; ++x)
+    for (int y = x + 1; y < 7; ++y)
+      if (overlap(bufs[x], sizes[x], bufs[y], sizes[y])) return HRM_ERR_ALIASING;
+  if (rope_table != nullptr) {
+    if (table_positions < position_offset + seq_len) return HRM_ERR_TABLE_RANGE;
+    const int64_t tbytes = mul_checked(mul_checked(table_positions, head_dim), 4);
+    if (tbytes < 0) return HRM_ERR_SIZE_OVERFLOW;
+    for (int x = 1; x < 7; ++x)
+      if (overlap(rope_table, tbytes, bufs[x], sizes[x])) return HRM_ERR_ALIASING;
+  }
+  return cuda_status(hrm::launch_split_rope(gqkv, gate_out, q_out, k_out, v_out, k_cache, v_cache, batch_size,
+                                            num_heads, seq_len, head_dim, position_offset, theta, rope_table,
+                                            cache ? cache_len : 0, cache ? cache_offset : 0, as_cuda(stream)));
+}
+
 }  // extern "C"

@@ -30,6 +30,10 @@ cudaError_t launch_embedding(const uint32_t* ids, const void* table, void* out, 
 
 cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                         int64_t offset, float theta, const float* table, cudaStream_t s);
+cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, void* v, void* kc, void* vc,
+                              int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t offset,
+                              float theta, const float* table, int64_t cache_len, int64_t cache_offset,
+                              cudaStream_t s);
 cudaError_t launch_rope_table(float* table, int64_t max_pos, int64_t head_dim, float theta, cudaStream_t s);
 
 }  // namespace hrm

@@ -98,6 +98,22 @@ __device__ __forceinline__ void rotate8(uint4& lo, uint4& hi, const float (&c)[8
   }
 }
 
+// cos/sin of pairs 8j..8j+7 at position pos: from the table or in-kernel.
+template <bool TABLE>
+__device__ __forceinline__ void load_cos_sin(const float4* table, int pos, int j, int head_dim, float theta,
+                                             float (&c)[8], float (&sn)[8]) {
+  if (TABLE) {
+    const float4* row = table + (int64_t)pos * (head_dim / 4);
+    const float4 c0 = ld_keep(row + 2 * j), c1 = ld_keep(row + 2 * j + 1);
+    const float4 s0 = ld_keep(row + head_dim / 8 + 2 * j), s1 = ld_keep(row + head_dim / 8 + 2 * j + 1);
+    c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+    sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sincosf(rope_angle(pos, 8 * j + e, head_dim, theta), &sn[e], &c[e]);
+  }
+}
+
 template <bool TABLE>
 __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel(const RopeArgs a) {
   const int j = threadIdx.x % a.g;
@@ -113,16 +129,7 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel
     const int pos = (int)s + a.offset;
 
     float c[8], sn[8];
-    if (TABLE) {
-      const float4* row = a.table + (int64_t)pos * (a.head_dim / 4);
-      const float4 c0 = ld_keep(row + 2 * j), c1 = ld_keep(row + 2 * j + 1);
-      const float4 s0 = ld_keep(row + a.head_dim / 8 + 2 * j), s1 = ld_keep(row + a.head_dim / 8 + 2 * j + 1);
-      c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
-      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) sincosf(rope_angle(pos, 8 * j + e, a.head_dim, a.theta), &sn[e], &c[e]);
-    }
+    load_cos_sin<TABLE>(a.table, pos, j, a.head_dim, a.theta, c, sn);
 
     // Chunk index of (b, h, s) row start: ((b * heads + h) * seq + s) * row_chunks.
     const int64_t head_step = a.seq * row_chunks;
@@ -207,6 +214,135 @@ __global__ void __launch_bounds__(256) rope_table_kernel(float* table, int64_t p
   }
 }
 
+// ---------------------------------------------------- split + RoPE + cache
+// The attention prologue of the reference reads the projection output
+// [batch, seq, 4*heads*head_dim] three times over three kernels (split_gqkv,
+// rope_embed, kv_cache_update).  Here one thread moves, per head it visits,
+// the 8 pairs it owns of all four segments: gate and v are copied, q and k
+// rotated with the cos/sin it fetched once, and k / v also go to the cache.
+// Same tile shape as rope_tile_kernel.
+struct SplitArgs {
+  const uint4* gqkv;
+  uint4* gate;
+  uint4* q;
+  uint4* k;
+  uint4* v;
+  uint4* kc;  // k cache or null
+  uint4* vc;  // v cache or null
+  const float4* table;
+  int64_t seq;
+  int64_t tiles_per_batch;
+  int64_t ntiles;
+  int64_t cache_len;
+  int64_t cache_offset;
+  int heads;
+  int head_dim;
+  int g, pt, ht;
+  int offset;
+  float theta;
+};
+
+template <bool TABLE, bool CACHE>
+__global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) split_rope_tile_kernel(const SplitArgs a) {
+  const int j = threadIdx.x % a.g;
+  const int rest = threadIdx.x / a.g;
+  const int slice = rest % a.ht;
+  const int pl = rest / a.ht;
+  const int row_chunks = 2 * a.g;                       // 16-byte chunks per head row
+  const int64_t seg = (int64_t)a.heads * row_chunks;   // chunks per gqkv segment
+
+  for (int64_t tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
+    const int64_t b = tile / a.tiles_per_batch;
+    const int64_t s = (tile - b * a.tiles_per_batch) * a.pt + pl;
+    if (s >= a.seq) continue;
+    float c[8], sn[8];
+    load_cos_sin<TABLE>(a.table, (int)s + a.offset, j, a.head_dim, a.theta, c, sn);
+
+    const int64_t tok = b * a.seq + s;
+    const int64_t in0 = tok * 4 * seg + j;                              // + h * row_chunks
+    const int64_t gate0 = tok * seg + j;                                // + h * row_chunks
+    const int64_t out0 = ((b * a.heads) * a.seq + s) * row_chunks + j;  // + h * out_step
+    const int64_t out_step = a.seq * row_chunks;
+    const int64_t c0 = ((b * a.heads) * a.cache_len + a.cache_offset + s) * row_chunks + j;
+    const int64_t c_step = a.cache_len * row_chunks;
+    for (int h = slice; h < a.heads; h += a.ht) {
+      const int64_t src = in0 + (int64_t)h * row_chunks;
+      const uint4 gl = ld_stream(a.gqkv + src), gh = ld_stream(a.gqkv + src + a.g);
+      uint4 ql = ld_stream(a.gqkv + src + seg), qh = ld_stream(a.gqkv + src + seg + a.g);
+      uint4 kl = ld_stream(a.gqkv + src + 2 * seg), kh = ld_stream(a.gqkv + src + 2 * seg + a.g);
+      const uint4 vl = ld_stream(a.gqkv + src + 3 * seg), vh = ld_stream(a.gqkv + src + 3 * seg + a.g);
+      rotate8<false>(ql, qh, c, sn);
+      rotate8<true>(kl, kh, c, sn);
+      const int64_t go = gate0 + (int64_t)h * row_chunks, o = out0 + (int64_t)h * out_step;
+      st_stream(a.gate + go, gl);
+      st_stream(a.gate + go + a.g, gh);
+      st_stream(a.q + o, ql);
+      st_stream(a.q + o + a.g, qh);
+      st_stream(a.k + o, kl);
+      st_stream(a.k + o + a.g, kh);
+      st_stream(a.v + o, vl);
+      st_stream(a.v + o + a.g, vh);
+      if (CACHE) {
+        const int64_t co = c0 + (int64_t)h * c_step;
+        st_stream(a.kc + co, kl);
+        st_stream(a.kc + co + a.g, kh);
+        st_stream(a.vc + co, vl);
+        st_stream(a.vc + co + a.g, vh);
+      }
+    }
+  }
+}
+
+// Any even head_dim / alignment: one thread per (b, h, s, pair).
+__global__ void __launch_bounds__(256) split_rope_scalar_kernel(
+    const uint16_t* gqkv, uint16_t* gate, uint16_t* q, uint16_t* k, uint16_t* v, uint16_t* kc, uint16_t* vc,
+    int64_t batch, int64_t seq, int heads, int head_dim, int offset, float theta, const float* table,
+    int64_t cache_len, int64_t cache_offset) {
+  const int half = head_dim / 2;
+  const int64_t total = batch * heads * seq * half;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+    const int i = (int)(idx % half);
+    const int64_t r = idx / half;
+    const int64_t s = r % seq;
+    const int64_t bh = r / seq;
+    const int h = (int)(bh % heads);
+    const int64_t b = bh / heads;
+    const int pos = (int)s + offset;
+    float c, sn;
+    if (table != nullptr) {
+      c = table[(int64_t)pos * head_dim + i];
+      sn = table[(int64_t)pos * head_dim + half + i];
+    } else {
+      sincosf(rope_angle(pos, i, head_dim, theta), &sn, &c);
+    }
+    const int64_t tok = b * seq + s;
+    const int64_t in = tok * 4 * heads * head_dim + (int64_t)h * head_dim + i;
+    const int64_t segd = (int64_t)heads * head_dim;
+    const int64_t go = (tok * heads + h) * head_dim + i;
+    const int64_t o = ((b * heads + h) * seq + s) * head_dim + i;
+    gate[go] = gqkv[in];
+    gate[go + half] = gqkv[in + half];
+    const float x0 = bf16_to_f32(gqkv[in + segd]), x1 = bf16_to_f32(gqkv[in + segd + half]);
+    q[o] = f32_to_bf16(rot_lo(x0, x1, c, sn));
+    q[o + half] = f32_to_bf16(rot_hi_q(x0, x1, c, sn));
+    const float k0 = bf16_to_f32(gqkv[in + 2 * segd]), k1 = bf16_to_f32(gqkv[in + 2 * segd + half]);
+    const uint16_t klo = f32_to_bf16(rot_lo(k0, k1, c, sn)), khi = f32_to_bf16(rot_hi_k(k0, k1, c, sn));
+    k[o] = klo;
+    k[o + half] = khi;
+    const uint16_t vlo = gqkv[in + 3 * segd], vhi = gqkv[in + 3 * segd + half];
+    v[o] = vlo;
+    v[o + half] = vhi;
+    if (kc != nullptr) {
+      const int64_t co = ((b * heads + h) * cache_len + cache_offset + s) * head_dim + i;
+      kc[co] = klo;
+      kc[co + half] = khi;
+      vc[co] = vlo;
+      vc[co + half] = vhi;
+    }
+  }
+}
+
 int pow2_ceil(int64_t x) {
   int p = 1;
   while (p < x && p < (1 << 30)) p <<= 1;
@@ -259,6 +395,63 @@ cudaError_t launch_rope_table(float* table, int64_t positions, int64_t head_dim,
   const int64_t cap = (int64_t)device_sm_count() * 8;
   if (blocks > cap) blocks = cap;
   rope_table_kernel<<<(unsigned)blocks, 256, 0, s>>>(table, positions, (int)head_dim, theta);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, void* v, void* kc, void* vc,
+                              int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t offset,
+                              float theta, const float* table, int64_t cache_len, int64_t cache_offset,
+                              cudaStream_t s) {
+  const int64_t sms = device_sm_count();
+  const int g = (int)(head_dim / 16);
+  const bool fast = head_dim % 16 == 0 && head_dim <= 512 && (g & (g - 1)) == 0 && aligned16(gqkv) &&
+                    aligned16(gate) && aligned16(q) && aligned16(k) && aligned16(v) &&
+                    (kc == nullptr || (aligned16(kc) && aligned16(vc))) && (table == nullptr || aligned16(table));
+  if (fast) {
+    SplitArgs a;
+    a.gqkv = static_cast<const uint4*>(gqkv);
+    a.gate = static_cast<uint4*>(gate);
+    a.q = static_cast<uint4*>(q);
+    a.k = static_cast<uint4*>(k);
+    a.v = static_cast<uint4*>(v);
+    a.kc = static_cast<uint4*>(kc);
+    a.vc = static_cast<uint4*>(vc);
+    a.table = reinterpret_cast<const float4*>(table);
+    a.seq = seq;
+    a.heads = (int)heads;
+    a.head_dim = (int)head_dim;
+    a.g = g;
+    a.pt = pow2_ceil(seq);
+    if (a.pt > kThreads / g) a.pt = kThreads / g;
+    a.ht = kThreads / (g * a.pt);
+    a.tiles_per_batch = (seq + a.pt - 1) / a.pt;
+    a.ntiles = batch * a.tiles_per_batch;
+    a.cache_len = cache_len;
+    a.cache_offset = cache_offset;
+    a.offset = (int)offset;
+    a.theta = theta;
+    int64_t blocks = a.ntiles;
+    if (HRM_ROPE_CAP > 0 && blocks > sms * HRM_ROPE_CAP) blocks = sms * HRM_ROPE_CAP;
+    if (blocks > INT32_MAX) blocks = INT32_MAX;
+    if (table != nullptr) {
+      if (kc != nullptr)
+        split_rope_tile_kernel<true, true><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+      else
+        split_rope_tile_kernel<true, false><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+    } else {
+      if (kc != nullptr)
+        split_rope_tile_kernel<false, true><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+      else
+        split_rope_tile_kernel<false, false><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+    }
+  } else {
+    int64_t blocks = (batch * heads * seq * (head_dim / 2) + 255) / 256;
+    if (blocks > sms * 8) blocks = sms * 8;
+    split_rope_scalar_kernel<<<(unsigned)blocks, 256, 0, s>>>(
+        static_cast<const uint16_t*>(gqkv), static_cast<uint16_t*>(gate), static_cast<uint16_t*>(q),
+        static_cast<uint16_t*>(k), static_cast<uint16_t*>(v), static_cast<uint16_t*>(kc), static_cast<uint16_t*>(vc),
+        batch, seq, (int)heads, (int)head_dim, (int)offset, theta, table, cache_len, cache_offset);
+  }
   return cudaGetLastError();
 }
 

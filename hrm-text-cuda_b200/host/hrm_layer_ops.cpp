@@ -183,6 +183,34 @@ void HrmLayerOps::embed_rms_norm(const CudaSlice<uint32_t>& input_ids, const Cud
         "embed_rms_norm");
 }
 
+void HrmLayerOps::split_gqkv_rope(const CudaSlice<bf16>& gqkv, CudaSlice<bf16>& gate, CudaSlice<bf16>& q,
+                                  CudaSlice<bf16>& k, CudaSlice<bf16>& v, CudaSlice<bf16>* k_cache,
+                                  CudaSlice<bf16>* v_cache, size_t batch_size, size_t seq_len, size_t num_heads,
+                                  size_t head_dim, size_t position_offset, size_t cache_len,
+                                  size_t cache_offset) const {
+  const size_t n = batch_size * seq_len * num_heads * head_dim;
+  need(gqkv, 4 * n, "split_gqkv_rope", "gqkv");
+  need(gate, n, "split_gqkv_rope", "gate");
+  need(q, n, "split_gqkv_rope", "q");
+  need(k, n, "split_gqkv_rope", "k");
+  need(v, n, "split_gqkv_rope", "v");
+  if ((k_cache == nullptr) != (v_cache == nullptr))
+    fail(HrmError::Kind::InvalidInput, HRM_ERR_NULL_POINTER, "split_gqkv_rope: pass both caches or neither");
+  if (k_cache) {
+    need(*k_cache, batch_size * num_heads * cache_len * head_dim, "split_gqkv_rope", "k_cache");
+    need(*v_cache, batch_size * num_heads * cache_len * head_dim, "split_gqkv_rope", "v_cache");
+  }
+  const bool use_table = rope_table_.device_ptr() != nullptr && head_dim == config.head_dim &&
+                         position_offset + seq_len <= rope_positions_;
+  check(hrm_split_gqkv_rope(gqkv.device_ptr(), gate.device_ptr(), q.device_ptr(), k.device_ptr(), v.device_ptr(),
+                            k_cache ? k_cache->device_ptr() : nullptr, v_cache ? v_cache->device_ptr() : nullptr,
+                            (int64_t)batch_size, (int64_t)seq_len, (int64_t)num_heads, (int64_t)head_dim,
+                            (int64_t)position_offset, config.rope_theta,
+                            use_table ? rope_table_.device_ptr() : nullptr, use_table ? (int64_t)rope_positions_ : 0,
+                            (int64_t)cache_len, (int64_t)cache_offset, stream_),
+        "split_gqkv_rope");
+}
+
 void HrmLayerOps::build_rope_table(size_t max_positions) {
   void* p = nullptr;
   const size_t n = max_positions * config.head_dim;

@@ -122,6 +122,12 @@ class HrmLayerOps {
   void embed_rms_norm(const CudaSlice<uint32_t>& input_ids, const CudaSlice<bf16>& embedding_table,
                       CudaSlice<bf16>* hidden_out, CudaSlice<bf16>& normed_out, const CudaSlice<bf16>* weight,
                       size_t rows, size_t hidden_size, size_t vocab_size, float embedding_scale) const;
+  // split_gqkv -> rope_embed -> kv_cache_update in one pass (src/lib.rs:798-857);
+  // k_cache / v_cache ([batch, heads, cache_len, head_dim]) may both be null.
+  void split_gqkv_rope(const CudaSlice<bf16>& gqkv, CudaSlice<bf16>& gate, CudaSlice<bf16>& q, CudaSlice<bf16>& k,
+                       CudaSlice<bf16>& v, CudaSlice<bf16>* k_cache, CudaSlice<bf16>* v_cache, size_t batch_size,
+                       size_t seq_len, size_t num_heads, size_t head_dim, size_t position_offset, size_t cache_len,
+                       size_t cache_offset) const;
   // Builds the fp32 cos/sin table for config.head_dim / config.rope_theta
   // covering positions [0, max_positions); rope_embed uses it from then on
   // for every call it covers, and evaluates angles in-kernel otherwise.

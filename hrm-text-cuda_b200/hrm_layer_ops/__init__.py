@@ -13,6 +13,7 @@ from .ops import (  # noqa: F401
     rms_norm,
     rope_embed,
     rope_table,
+    split_gqkv_rope,
     swiglu_ffn,
 )
 
@@ -26,4 +27,5 @@ __all__ = [
     "rope_embed",
     "embedding_lookup",
     "embed_rms_norm",
+    "split_gqkv_rope",
 ]

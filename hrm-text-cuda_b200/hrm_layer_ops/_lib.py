@@ -36,6 +36,8 @@ SIGNATURES = {
     "hrm_swiglu_ffn": [_p, _p, _p, _i64, _p],
     "hrm_embedding_lookup": [_p, _p, _p, _i64, _i64, _i64, _i64, _f32, _p],
     "hrm_embed_rms_norm": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f32, _f32, _p],
+    "hrm_split_gqkv_rope": [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _i64,
+                            _i64, _p],
     "hrm_abi_version": [],
 }
 

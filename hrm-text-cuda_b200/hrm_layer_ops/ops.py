@@ -192,3 +192,40 @@ def embed_rms_norm(ids: torch.Tensor, table: torch.Tensor, embedding_scale: floa
     call("hrm_embed_rms_norm", _ptr(ids), _ptr(table), _ptr(hidden_out), _ptr(normed_out), _ptr(weight),
          ids.numel(), hidden, vocab, embedding_scale, eps, _stream(table, stream))
     return hidden_out, normed_out
+
+
+def split_gqkv_rope(gqkv: torch.Tensor, num_heads: int, position_offset: int = 0, theta: float = 10000.0,
+                    table: Optional[torch.Tensor] = None, k_cache: Optional[torch.Tensor] = None,
+                    v_cache: Optional[torch.Tensor] = None, cache_offset: int = 0, out=None, *, stream=None):
+    """Split + RoPE + KV-cache write in one pass over gqkv [batch, seq, 4 * heads * head_dim].
+
+    Returns (gate [b, s, h, d], q, k, v [b, h, s, d]); with k_cache / v_cache
+    ([b, h, cache_len, d]) the rotated k and v are also written at rows
+    cache_offset + s.  Replaces split_gqkv -> rope_embed -> kv_cache_update
+    (src/lib.rs:798-857).
+    """
+    _need(gqkv, "gqkv")
+    if gqkv.dim() != 3 or gqkv.shape[2] % (4 * num_heads):
+        raise ValueError("gqkv must be [batch, seq, 4 * heads * head_dim]")
+    b, s, w = gqkv.shape
+    d = w // (4 * num_heads)
+    if out is None:
+        out = (torch.empty((b, s, num_heads, d), dtype=gqkv.dtype, device=gqkv.device),
+               *(torch.empty((b, num_heads, s, d), dtype=gqkv.dtype, device=gqkv.device) for _ in range(3)))
+    for t, n in zip(out, ("gate", "q", "k", "v")):
+        _need(t, n)
+    positions, cache_len = 0, 0
+    if table is not None:
+        _need(table, "table", (torch.float32,))
+        positions = table.shape[0]
+    if (k_cache is None) != (v_cache is None):
+        raise ValueError("pass both k_cache and v_cache or neither")
+    if k_cache is not None:
+        _need(k_cache, "k_cache"); _need(v_cache, "v_cache")
+        if k_cache.dim() != 4 or k_cache.shape != v_cache.shape or k_cache.shape[:2] != (b, num_heads):
+            raise ValueError("caches must be [batch, heads, cache_len, head_dim]")
+        cache_len = k_cache.shape[2]
+    call("hrm_split_gqkv_rope", _ptr(gqkv), *(_ptr(t) for t in out), _ptr(k_cache), _ptr(v_cache), b, s,
+         num_heads, d, position_offset, theta, _ptr(table), positions, cache_len, cache_offset,
+         _stream(gqkv, stream))
+    return out

@@ -146,6 +146,31 @@ int hrm_embed_rms_norm(const uint32_t* input_ids, const void* embedding_table,
                        int64_t rows, int64_t hidden_size, int64_t vocab_size,
                        float embedding_scale, float eps, hrm_stream_t stream);
 
+/* Fused attention-input preparation: split + RoPE + KV-cache write, reading
+ * the projection output once.
+ *   gqkv      [batch, seq, 4*heads*head_dim] bf16; per token the heads are laid
+ *             out [gate heads | q heads | k heads | v heads]
+ *   gate_out  [batch, seq, heads, head_dim]        copy of the gate heads
+ *   q_out, k_out, v_out [batch, heads, seq, head_dim]; q and k rotated exactly
+ *             as hrm_rope_embed does at position_offset (rope_table optional,
+ *             same rules), v copied
+ *   k_cache, v_cache: both NULL (no cache write) or both [batch, heads,
+ *             cache_len, head_dim]; the rotated k and the v of token s are
+ *             also written at cache position cache_offset + s
+ *             (cache_offset + seq_len <= cache_len)
+ * Replaces split_gqkv (src/lib.rs:567-605, src/kernels/split_gqkv.cu:10-49)
+ * -> rope_embed (src/lib.rs:821-836) -> kv_cache_update (src/lib.rs:706-747,
+ * src/kernels/kv_cache_update.cu:12-48) as the attention prologue runs them
+ * (src/lib.rs:798-857 and 900-916; prefill writes the cache at 0, decode at
+ * cached_len, which is also its position_offset).  Outputs are bit-identical
+ * to that three-kernel sequence.  head_dim must be even; no two buffers may
+ * overlap.                                                                  */
+int hrm_split_gqkv_rope(const void* gqkv, void* gate_out, void* q_out, void* k_out, void* v_out,
+                        void* k_cache, void* v_cache, int64_t batch_size, int64_t seq_len,
+                        int64_t num_heads, int64_t head_dim, int64_t position_offset, float theta,
+                        const float* rope_table, int64_t table_positions, int64_t cache_len,
+                        int64_t cache_offset, hrm_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -220,3 +220,33 @@ void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int6
     }
   }
 }
+
+/* split_gqkv.cu:27-48 */
+void ora_split_gqkv(const uint16_t* gqkv, uint16_t* gate, uint16_t* q, uint16_t* k, uint16_t* v, int64_t batch,
+                    int64_t seq, int64_t heads, int64_t head_dim) {
+#pragma omp parallel for schedule(static)
+  for (int64_t tok = 0; tok < batch * seq; ++tok) {
+    const int64_t b = tok / seq, s = tok % seq;
+    const uint16_t* in = gqkv + tok * 4 * heads * head_dim;
+    for (int64_t h = 0; h < heads; ++h) {
+      const int64_t o = ((b * heads + h) * seq + s) * head_dim;
+      memcpy(gate + (tok * heads + h) * head_dim, in + h * head_dim, (size_t)head_dim * 2);
+      memcpy(q + o, in + (heads + h) * head_dim, (size_t)head_dim * 2);
+      memcpy(k + o, in + (2 * heads + h) * head_dim, (size_t)head_dim * 2);
+      memcpy(v + o, in + (3 * heads + h) * head_dim, (size_t)head_dim * 2);
+    }
+  }
+}
+
+/* kv_cache_update.cu:78-95 */
+void ora_kv_cache_update(const uint16_t* k, const uint16_t* v, uint16_t* k_cache, uint16_t* v_cache, int64_t batch,
+                         int64_t heads, int64_t seq, int64_t head_dim, int64_t max_len, int64_t cached_len,
+                         int is_decode) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < batch * heads * seq; ++r) {
+    const int64_t bh = r / seq, s = r % seq;
+    const int64_t pos = is_decode ? cached_len + s : s;
+    memcpy(k_cache + (bh * max_len + pos) * head_dim, k + r * head_dim, (size_t)head_dim * 2);
+    memcpy(v_cache + (bh * max_len + pos) * head_dim, v + r * head_dim, (size_t)head_dim * 2);
+  }
+}

@@ -58,6 +58,17 @@ void ora_rope_table(float* table, int64_t positions, int64_t head_dim, float the
 void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                     int64_t offset, float theta, const float* table);
 
+/* split_gqkv.cu:27-48: per token [gate | q | k | v] heads -> gate [b, s, h, :],
+ * q, k, v [b, h, s, :] (plain copies). */
+void ora_split_gqkv(const uint16_t* gqkv, uint16_t* gate, uint16_t* q, uint16_t* k, uint16_t* v, int64_t batch,
+                    int64_t seq, int64_t heads, int64_t head_dim);
+
+/* kv_cache_update.cu:78-95: [b, h, s, :] -> cache [b, h, max_len, :] at row
+ * s (prefill) or cached_len + s (decode). */
+void ora_kv_cache_update(const uint16_t* k, const uint16_t* v, uint16_t* k_cache, uint16_t* v_cache, int64_t batch,
+                         int64_t heads, int64_t seq, int64_t head_dim, int64_t max_len, int64_t cached_len,
+                         int is_decode);
+
 #ifdef __cplusplus
 }
 #endif

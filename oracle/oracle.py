@@ -79,6 +79,8 @@ class Oracle:
         "ora_embed_rms_norm": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f32, _f32],
         "ora_rope_table": [_p, _i64, _i64, _f32],
         "ora_rope_embed": [_p, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p],
+        "ora_split_gqkv": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64],
+        "ora_kv_cache_update": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int],
         "ora_set_threads": [ctypes.c_int],
     }
 
@@ -170,6 +172,35 @@ class Oracle:
         return q, k
 
 
+    def split_gqkv(self, gqkv, batch, seq, heads, head_dim):
+        gqkv = self._c(gqkv, np.uint16)
+        gate = np.empty((batch, seq, heads, head_dim), np.uint16)
+        q, k, v = (np.empty((batch, heads, seq, head_dim), np.uint16) for _ in range(3))
+        self.lib.ora_split_gqkv(self._ptr(gqkv), self._ptr(gate), self._ptr(q), self._ptr(k), self._ptr(v), batch,
+                                seq, heads, head_dim)
+        return gate, q, k, v
+
+    def kv_cache_update(self, k, v, k_cache, v_cache, cached_len, is_decode):
+        """Writes into copies of the caches and returns them."""
+        k, v = self._c(k, np.uint16), self._c(v, np.uint16)
+        kc, vc = np.array(k_cache, np.uint16, copy=True), np.array(v_cache, np.uint16, copy=True)
+        b, h, s, d = k.shape
+        self.lib.ora_kv_cache_update(self._ptr(k), self._ptr(v), self._ptr(kc), self._ptr(vc), b, h, s, d,
+                                     kc.shape[2], cached_len, int(is_decode))
+        return kc, vc
+
+    def split_gqkv_rope(self, gqkv, batch, seq, heads, head_dim, offset, theta=10000.0, table=None,
+                        k_cache=None, v_cache=None, cache_offset=0):
+        """The reference's attention prologue: split -> rope -> kv_cache_update."""
+        gate, q, k, v = self.split_gqkv(gqkv, batch, seq, heads, head_dim)
+        q, k = self.rope_embed(q, k, offset, theta, table)
+        kc = vc = None
+        if k_cache is not None:
+            # the reference writes at s (prefill, offset 0) or cached_len + s (decode)
+            kc, vc = self.kv_cache_update(k, v, k_cache, v_cache, cache_offset, True)
+        return gate, q, k, v, kc, vc
+
+
 # ------------------------------------------------- reference kernels (GPU)
 class RefKernels:
     """The reference's kernels, built from its sources; torch CUDA tensors in."""
@@ -180,6 +211,8 @@ class RefKernels:
         "ref_rope_embed": [_p, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p],
         "ref_swiglu_ffn": [_p, _p, _p, _i64, _p],
         "ref_embedding_lookup": [_p, _p, _p, _i64, _i64, _i64, _i64, _f32, _p],
+        "ref_split_gqkv": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
+        "ref_kv_cache_update": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _p],
     }
 
     def __init__(self, path: str = REF_LIB):
@@ -220,3 +253,13 @@ class RefKernels:
         vocab, hidden = table.shape
         self._run("ref_embedding_lookup", _p(ids.data_ptr()), _p(table.data_ptr()), _p(out.data_ptr()), 1,
                   ids.numel(), hidden, vocab, scale)
+
+    def split_gqkv(self, gqkv, gate, q, k, v):
+        b, h, s, d = q.shape
+        self._run("ref_split_gqkv", _p(gqkv.data_ptr()), _p(gate.data_ptr()), _p(q.data_ptr()), _p(k.data_ptr()),
+                  _p(v.data_ptr()), b, s, h, d)
+
+    def kv_cache_update(self, k, v, k_cache, v_cache, cached_len, is_decode):
+        b, h, s, d = k.shape
+        self._run("ref_kv_cache_update", _p(k.data_ptr()), _p(v.data_ptr()), _p(k_cache.data_ptr()),
+                  _p(v_cache.data_ptr()), b, h, s, d, k_cache.shape[2], cached_len, int(is_decode))

@@ -10,8 +10,10 @@
 
 #include "additive_inject.cu"
 #include "embedding_lookup.cu"
+#include "kv_cache_update.cu"
 #include "rms_norm.cu"
 #include "rope_embed.cu"
+#include "split_gqkv.cu"
 #include "swiglu_ffn.cu"
 
 namespace {
@@ -58,6 +60,29 @@ int ref_embedding_lookup(const uint32_t* ids, const void* table, void* out, int6
   const unsigned blocks = blocks_for(batch * seq * (hidden / 8), 256);
   embedding_lookup_kernel<<<blocks, 256, 0, s>>>(ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, (int)batch,
                                                  (int)seq, (int)hidden, (int)vocab, scale);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:579-602
+int ref_split_gqkv(const void* gqkv, void* gate, void* q, void* k, void* v, int64_t batch, int64_t seq,
+                   int64_t heads, int64_t head_dim, cudaStream_t s) {
+  const unsigned blocks = blocks_for(batch * seq * heads * (head_dim / 8), 256);
+  split_gqkv_kernel<<<blocks, 256, 0, s>>>((const __nv_bfloat16*)gqkv, (__nv_bfloat16*)gate, (__nv_bfloat16*)q,
+                                           (__nv_bfloat16*)k, (__nv_bfloat16*)v, (int)batch, (int)seq, (int)heads,
+                                           (int)head_dim);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:719-744
+int ref_kv_cache_update(const void* k, const void* v, void* kc, void* vc, int64_t batch, int64_t heads, int64_t seq,
+                        int64_t head_dim, int64_t max_len, int64_t cached_len, int is_decode, cudaStream_t s) {
+  int64_t blocks = (batch * heads * seq * head_dim + 255) / 256;
+  if (blocks > 65535) blocks = 65535;
+  if (blocks < 1) blocks = 1;
+  kv_cache_update_kernel<<<(unsigned)blocks, 256, 0, s>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+                                                          (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, (int)batch,
+                                                          (int)heads, (int)seq, (int)head_dim, (int)max_len,
+                                                          (int)cached_len, is_decode);
   return (int)cudaGetLastError();
 }
 

@@ -121,6 +121,43 @@ void test_add_rms_norm(HrmLayerOps& hrm) {
   }
 }
 
+// split_gqkv_rope == rope_embed applied to the q / k segments of gqkv, and the
+// cache rows at the offset hold the rotated k and the v.
+void test_split_gqkv_rope(HrmLayerOps& hrm) {
+  const size_t b = 1, s = 3, h = 2, d = 128, off = 5, cache_len = 9, n = b * s * h * d;
+  std::vector<float> g(4 * n);
+  for (size_t i = 0; i < g.size(); ++i) g[i] = std::sin(0.01f * (float)i);
+  auto hg = to_bf16(g);
+  auto dg = hrm.htod_copy_bf16(hg);
+  auto gate = hrm.alloc_zero_bf16(n), q = hrm.alloc_zero_bf16(n), k = hrm.alloc_zero_bf16(n);
+  auto v = hrm.alloc_zero_bf16(n);
+  auto kc = hrm.alloc_zero_bf16(b * h * cache_len * d), vc = hrm.alloc_zero_bf16(b * h * cache_len * d);
+  hrm.split_gqkv_rope(dg, gate, q, k, v, &kc, &vc, b, s, h, d, off, cache_len, off);
+  // reference path: the q / k segments copied into [b, h, s, d] and rotated by rope_embed
+  std::vector<bf16> hq(n), hk(n);
+  for (size_t t = 0; t < s; ++t)
+    for (size_t hh = 0; hh < h; ++hh)
+      for (size_t i = 0; i < d; ++i) {
+        hq[(hh * s + t) * d + i] = hg[t * 4 * h * d + (h + hh) * d + i];
+        hk[(hh * s + t) * d + i] = hg[t * 4 * h * d + (2 * h + hh) * d + i];
+      }
+  auto rq = hrm.htod_copy_bf16(hq), rk = hrm.htod_copy_bf16(hk);
+  hrm.rope_embed(rq, rk, b, h, s, d, off);
+  auto q1 = hrm.sync_reclaim(std::move(q)), q2 = hrm.sync_reclaim(std::move(rq));
+  auto k1 = hrm.sync_reclaim(std::move(k)), k2 = hrm.sync_reclaim(std::move(rk));
+  auto v1 = hrm.sync_reclaim(std::move(v)), kc1 = hrm.sync_reclaim(std::move(kc)), vc1 = hrm.sync_reclaim(std::move(vc));
+  for (size_t i = 0; i < n; ++i) {
+    expect(q1[i].bits == q2[i].bits, "split_gqkv_rope q");
+    expect(k1[i].bits == k2[i].bits, "split_gqkv_rope k");
+  }
+  for (size_t hh = 0; hh < h; ++hh)
+    for (size_t t = 0; t < s; ++t)
+      for (size_t i = 0; i < d; ++i) {
+        expect(kc1[(hh * cache_len + off + t) * d + i].bits == k1[(hh * s + t) * d + i].bits, "k cache row");
+        expect(vc1[(hh * cache_len + off + t) * d + i].bits == v1[(hh * s + t) * d + i].bits, "v cache row");
+      }
+}
+
 // Argument errors come back as HrmError::InvalidInput, not as a launch.
 void test_invalid_input(HrmLayerOps& hrm) {
   auto a = hrm.alloc_zero_bf16(4);
@@ -148,6 +185,7 @@ int main() {
       {"test_additive_inject", test_additive_inject}, {"test_rms_norm", test_rms_norm},
       {"test_swiglu_ffn", test_swiglu_ffn},           {"test_embedding_lookup", test_embedding_lookup},
       {"test_rope_embed", test_rope_embed},           {"test_add_rms_norm", test_add_rms_norm},
+      {"test_split_gqkv_rope", test_split_gqkv_rope},
       {"test_invalid_input", test_invalid_input},
   };
   try {

@@ -18,4 +18,4 @@ def test_cpp_host_known_answers():
     res = subprocess.run([exe], capture_output=True, text=True, timeout=120)
     print(res.stdout)
     assert res.returncode == 0, res.stdout + res.stderr
-    assert "all 7 tests passed" in res.stdout
+    assert "all 8 tests passed" in res.stdout

@@ -229,3 +229,44 @@ def test_rope_table_range_error(cuda):
     q = torch.zeros((1, 1, 4, 128), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(ops.HrmError):
         ops.rope_embed(q, q.clone(), 10, 10000.0, ops.rope_table(12, 128))
+
+
+# -------------------------------------------------- split + RoPE + KV cache
+SPLIT_CASES = [(2, 300, 4, 128, 0, True), (8, 1, 16, 128, 4095, True), (1, 33, 12, 128, 0, False),
+               (1, 7, 3, 64, 5, True), (1, 5, 2, 96, 0, True), (1, 3, 2, 130, 2, False)]
+
+
+@pytest.mark.parametrize("b,s,h,d,off,with_cache", SPLIT_CASES)
+@pytest.mark.parametrize("use_table", [False, True])
+def test_split_gqkv_rope(oracle, rng, cuda, b, s, h, d, off, with_cache, use_table):
+    """Fused split + RoPE + cache write vs the oracle's split -> rope -> kv_cache_update:
+    copies (gate, v, cache rows) bit-exact, rotated q/k <= 2 bf16 ulp at pair magnitude,
+    cache rows outside [off, off + s) untouched."""
+    gqkv = normal_bf16(rng, (b, s, 4 * h * d))
+    cache_len = off + s + 3
+    kc0, vc0 = normal_bf16(rng, (b, h, cache_len, d)), normal_bf16(rng, (b, h, cache_len, d))
+    dkc, dvc = (to_dev(kc0, cuda), to_dev(vc0, cuda)) if with_cache else (None, None)
+    table = ops.rope_table(off + s, d) if use_table else None
+    gate, q, k, v = ops.split_gqkv_rope(to_dev(gqkv, cuda), h, off, 10000.0, table, dkc, dvc, cache_offset=off)
+    wg, wq, wk, wv, wkc, wvc = oracle.split_gqkv_rope(gqkv, b, s, h, d, off, 10000.0, None, kc0, vc0, off)
+    assert_bits_equal(to_host(gate), wg, "gate")
+    assert_bits_equal(to_host(v), wv, "v")
+    for got, want in ((to_host(q), wq), (to_host(k), wk)):
+        assert ulp_error(got, want, rope_pair_magnitude(want)).max() <= ULP_TOL
+    if with_cache:
+        hk, hv = to_host(dkc), to_host(dvc)
+        assert_bits_equal(hk[:, :, off:off + s], to_host(k), "k cache rows")
+        assert_bits_equal(hv[:, :, off:off + s], to_host(v), "v cache rows")
+        keep = np.ones(cache_len, bool)
+        keep[off:off + s] = False
+        assert_bits_equal(hk[:, :, keep], kc0[:, :, keep], "k cache untouched")
+        assert_bits_equal(hv[:, :, keep], vc0[:, :, keep], "v cache untouched")
+
+
+def test_split_gqkv_rope_errors(cuda):
+    g = torch.zeros((1, 4, 4 * 2 * 128), dtype=torch.bfloat16, device=cuda)
+    kc = torch.zeros((1, 2, 5, 128), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ops.HrmError):  # cache too short for offset 3 + seq 4
+        ops.split_gqkv_rope(g, 2, 3, 10000.0, None, kc, kc.clone(), cache_offset=3)
+    with pytest.raises(ValueError):
+        ops.split_gqkv_rope(g, 2, 0, 10000.0, None, kc, None)

@@ -146,6 +146,17 @@ def test_throughput_vs_reference_kernels(ref, cuda):
     res["rope_table"] = (nb / _time(lambda: ops.rope_embed(q, k, 0, 10000.0, table)), nb / t_ref)
     res["rope_in_kernel"] = (nb / _time(lambda: ops.rope_embed(q, k, 0, 10000.0, None)), nb / t_ref)
     del q, k
+    # split + RoPE + cache write: gqkv [16, 4096, 4 x 16 x 128] (65536 tokens) vs the
+    # reference's split_gqkv -> rope_embed -> kv_cache_update (bytes: the fused op's)
+    gq = rn((16, 4096, 4 * 16 * 128))
+    gate = torch.empty((16, 4096, 16, 128), dtype=bf, device=cuda)
+    qq, kk, vv, kc, vc = (torch.empty((16, 16, 4096, 128), dtype=bf, device=cuda) for _ in range(5))
+    nb = 65536 * 10 * 16 * 128 * 2
+    res["split_rope_cache"] = (
+        nb / _time(lambda: ops.split_gqkv_rope(gq, 16, 0, 10000.0, table, kc, vc, 0, out=(gate, qq, kk, vv))),
+        nb / _time(lambda: (ref.split_gqkv(gq, gate, qq, kk, vv), ref.rope_embed(qq, kk, 0, 10000.0),
+                            ref.kv_cache_update(kk, vv, kc, vc, 0, False))))
+    del gq, gate, qq, kk, vv, kc, vc
     # SwiGLU [32768 x 5632]
     gg, uu = rn((32768, 5632), 0.5), rn((32768, 5632), 0.5)
     oo = torch.empty_like(gg)
@@ -168,3 +179,24 @@ def test_throughput_vs_reference_kernels(ref, cuda):
             json.dump(out, f, indent=1)
     for k, v in out.items():
         assert v["speedup"] >= 0.95, (k, v)
+
+
+@pytest.mark.parametrize("b,s,h,d,off", [(2, 256, 16, 128, 0), (8, 1, 16, 128, 4095), (1, 77, 12, 64, 3)])
+@pytest.mark.parametrize("use_table", [False, True])
+def test_split_gqkv_rope_matches_reference_sequence(ref, rng, cuda, b, s, h, d, off, use_table):
+    """Fused op == the reference's split_gqkv -> rope_embed -> kv_cache_update (decode
+    form at cached_len = off), all outputs bit for bit."""
+    gqkv = to_dev(normal_bf16(rng, (b, s, 4 * h * d)), cuda)
+    cache_len = off + s + 2
+    kc0, vc0 = to_dev(normal_bf16(rng, (b, h, cache_len, d)), cuda), to_dev(normal_bf16(rng, (b, h, cache_len, d)), cuda)
+    rg = torch.empty((b, s, h, d), dtype=torch.bfloat16, device=cuda)
+    rq, rk, rv = (torch.empty((b, h, s, d), dtype=torch.bfloat16, device=cuda) for _ in range(3))
+    rkc, rvc = kc0.clone(), vc0.clone()
+    ref.split_gqkv(gqkv, rg, rq, rk, rv)
+    ref.rope_embed(rq, rk, off, 10000.0)
+    ref.kv_cache_update(rk, rv, rkc, rvc, off, True)
+    mkc, mvc = kc0.clone(), vc0.clone()
+    table = ops.rope_table(off + s, d) if use_table else None
+    outs = ops.split_gqkv_rope(gqkv, h, off, 10000.0, table, mkc, mvc, cache_offset=off)
+    for got, want, name in zip((*outs, mkc, mvc), (rg, rq, rk, rv, rkc, rvc), ("gate", "q", "k", "v", "kc", "vc")):
+        assert_bits_equal(to_host(got), to_host(want), name)
