@@ -291,6 +291,8 @@ class CpuChain:
         from hrm_layer_ops.chain import algorithmic_bytes_per_token
 
         self.o = o = Oracle()
+        # all the host cores this process may use (torchrun exports OMP_NUM_THREADS=1)
+        o.set_threads(len(os.sched_getaffinity(0)))
         rng = np.random.default_rng(0)
         self.tokens = T = CHAIN_S
 
