@@ -2,7 +2,8 @@
 """Throughput benchmark of the sm_100a per-token layer operators.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload chain|add_rms_norm|rms_norm_f32|rope|swiglu|embedding|split_rope]
+                    [--workload chain|add_rms_norm|rms_norm_f32|rope|swiglu|embedding|split_rope|
+                                attn_gate|convert_f32]
 
 Default workload ("chain"): the chained layer-op pass on 65536 tokens per GPU
 -- embedding [32000 x 2048] ~ N(0, 0.02) gathered for ids ~ U[0, 32000) and
@@ -61,7 +62,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="chain",
-                    choices=["chain", "add_rms_norm", "rms_norm_f32", "rope", "swiglu", "embedding", "split_rope"])
+                    choices=["chain", "add_rms_norm", "rms_norm_f32", "rope", "swiglu", "embedding", "split_rope",
+                             "attn_gate", "convert_f32"])
     ap.add_argument("--tokens", type=int, default=CHAIN_B * CHAIN_S,
                     help="chain tokens per GPU (a multiple of 4096; default 65536)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
@@ -372,6 +374,17 @@ class SingleOp:
                           *(torch.empty((B, HEADS, S, HEAD_DIM), dtype=bf, device=device) for _ in range(5)))
             self.cfg = {"workload": "split_gqkv + RoPE + KV-cache write, gqkv [16, 4096, 4 x 16 x 128] bf16",
                         "tokens": T}
+        elif name == "attn_gate":         # attn [65536 x 2048] *= sigmoid(gate), in place
+            shape = (65536, HIDDEN)
+            self.bytes_per_step, self.rows_per_step = 65536 * HIDDEN * 6, 65536
+            mk = lambda: (randn_bf16(shape, gen, device), randn_bf16(shape, gen, device))
+            self.cfg = {"workload": "attention gate in place [65536 x 2048] bf16", "rows": 65536}
+        elif name == "convert_f32":       # 2^28 f32 checkpoint values -> bf16 (a 1 GB tensor)
+            n = 1 << 28
+            self.bytes_per_step, self.rows_per_step = n * 6, n
+            mk = lambda: (torch.randn(n, generator=gen, device=device).view(torch.uint8),
+                          torch.empty(n, dtype=bf, device=device))
+            self.cfg = {"workload": "checkpoint f32 -> bf16 conversion, 2^28 values", "elements": n}
         else:
             raise ValueError(name)
         # Rotate input sets so that their total exceeds 3x L2: no step finds its inputs in L2.
@@ -399,6 +412,10 @@ class SingleOp:
             ops.rope_embed(b[0], b[1], 0, THETA, self.table, stream=stream)
         elif self.name == "swiglu":
             ops.swiglu_ffn(b[0], b[1], out=b[2], stream=stream)
+        elif self.name == "attn_gate":
+            ops.apply_attn_gate(b[0], b[1], stream=stream)
+        elif self.name == "convert_f32":
+            ops.convert_to_bf16(b[0], "f32", out=b[1], stream=stream)
         elif self.name == "split_rope":
             ops.split_gqkv_rope(b[0], HEADS, 0, THETA, self.table, b[5], b[6], 0, out=b[1:5], stream=stream)
         else:
@@ -412,8 +429,8 @@ class SingleOp:
         torch = self.torch
         b = self.bufs[0]
         n_in = {"add_rms_norm": 2, "rms_norm_f32": 1, "rope": 2, "swiglu": 2, "embedding": 1,
-                "split_rope": 1}[self.name]
-        outs = [0, 1] if self.name == "rope" else list(range(n_in, len(b)))
+                "split_rope": 1, "attn_gate": 2, "convert_f32": 1}[self.name]
+        outs = {"rope": [0, 1], "attn_gate": [1]}.get(self.name, list(range(n_in, len(b))))
         host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in b]
         for h, t in zip(host, b):
             h.copy_(t)

@@ -62,6 +62,7 @@ const char* hrm_status_string(int status) {
     case HRM_ERR_SIZE_OVERFLOW: return "size arithmetic overflows";
     case HRM_ERR_ALIASING: return "buffers that must be distinct overlap";
     case HRM_ERR_TABLE_RANGE: return "position_offset + seq_len exceeds the rope table";
+    case HRM_ERR_DTYPE: return "unsupported dtype";
     default: break;
   }
   if (status > HRM_ERR_CUDA) return cudaGetErrorString(static_cast<cudaError_t>(status - HRM_ERR_CUDA));
@@ -89,6 +90,31 @@ int hrm_swiglu_ffn(const void* gate, const void* up, void* output, int64_t total
   if (bytes < 0) return HRM_ERR_SIZE_OVERFLOW;
   if (partial_overlap(output, gate, bytes) || partial_overlap(output, up, bytes)) return HRM_ERR_ALIASING;
   return cuda_status(hrm::launch_swiglu(gate, up, output, total_elements, as_cuda(stream)));
+}
+
+int hrm_gated_attn_output(const void* gate, const void* attn_out, void* output, int64_t total_elements,
+                          hrm_stream_t stream) {
+  if (total_elements < 0) return HRM_ERR_INVALID_SHAPE;
+  if (total_elements == 0) return HRM_OK;
+  if (!gate || !attn_out || !output) return HRM_ERR_NULL_POINTER;
+  const int64_t bytes = mul_checked(total_elements, 2);
+  if (bytes < 0) return HRM_ERR_SIZE_OVERFLOW;
+  if (partial_overlap(output, attn_out, bytes) || overlap(output, bytes, gate, bytes)) return HRM_ERR_ALIASING;
+  return cuda_status(hrm::launch_attn_gate(gate, attn_out, output, total_elements, as_cuda(stream)));
+}
+
+int hrm_apply_attn_gate(const void* gate, void* attn_out, int64_t total_elements, hrm_stream_t stream) {
+  return hrm_gated_attn_output(gate, attn_out, attn_out, total_elements, stream);
+}
+
+int hrm_broadcast_vec(void* dst, const void* src, int64_t n_copies, int64_t vec_len, hrm_stream_t stream) {
+  if (n_copies < 0 || vec_len < 0) return HRM_ERR_INVALID_SHAPE;
+  if (n_copies == 0 || vec_len == 0) return HRM_OK;
+  if (!dst || !src) return HRM_ERR_NULL_POINTER;
+  const int64_t bytes = mul_checked(mul_checked(n_copies, vec_len), 2);
+  if (bytes < 0) return HRM_ERR_SIZE_OVERFLOW;
+  if (overlap(dst, bytes, src, vec_len * 2)) return HRM_ERR_ALIASING;
+  return cuda_status(hrm::launch_broadcast(dst, src, n_copies, vec_len, as_cuda(stream)));
 }
 
 int hrm_rms_norm(const void* input, void* output, const void* weight, int64_t rows, int64_t hidden_size,
@@ -232,6 +258,17 @@ int hrm_split_gqkv_rope(const void* gqkv, void* gate_out, void* q_out, void* k_o
   return cuda_status(hrm::launch_split_rope(gqkv, gate_out, q_out, k_out, v_out, k_cache, v_cache, batch_size,
                                             num_heads, seq_len, head_dim, position_offset, theta, rope_table,
                                             cache ? cache_len : 0, cache ? cache_offset : 0, as_cuda(stream)));
+}
+
+int hrm_convert_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, hrm_stream_t stream) {
+  if (src_dtype != HRM_DTYPE_BF16 && src_dtype != HRM_DTYPE_F32 && src_dtype != HRM_DTYPE_F16) return HRM_ERR_DTYPE;
+  if (n < 0) return HRM_ERR_INVALID_SHAPE;
+  if (n == 0) return HRM_OK;
+  if (!src || !dst) return HRM_ERR_NULL_POINTER;
+  const int64_t in_bytes = mul_checked(n, src_dtype == HRM_DTYPE_F32 ? 4 : 2), out_bytes = mul_checked(n, 2);
+  if (in_bytes < 0 || out_bytes < 0) return HRM_ERR_SIZE_OVERFLOW;
+  if (overlap(src, in_bytes, dst, out_bytes)) return HRM_ERR_ALIASING;
+  return cuda_status(hrm::launch_convert_to_bf16(src, src_dtype, dst, n, as_cuda(stream)));
 }
 
 }  // extern "C"

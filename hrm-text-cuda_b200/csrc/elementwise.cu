@@ -1,4 +1,5 @@
-// Elementwise bf16 streams: the SwiGLU gate and the residual add.
+// Elementwise bf16 streams: the SwiGLU gate, the residual add, the sigmoid
+// attention gate and the row broadcast.
 //
 // Both are pure HBM streams (2 reads + 1 write per element, ~0.5 flop/B), so
 // the kernel is shaped for bytes in flight, not arithmetic:
@@ -14,6 +15,7 @@
 // The arithmetic per element is the reference's, operation for operation:
 //   swiglu: g * (1.0f / (1.0f + __expf(-g))) * u    (src/kernels/swiglu_ffn.cu:31-35)
 //   add   : a + b                                   (src/kernels/additive_inject.cu:29-31)
+//   gate  : (1.0f / (1.0f + __expf(-g))) * a        (src/kernels/apply_attn_gate.cu:28-29)
 // each rounded once to bf16 (RNE), so results match the reference bit for bit.
 #include "common.cuh"
 #include "launch.h"
@@ -48,6 +50,26 @@ struct SwigluOp {
 struct AddOp {
   __device__ __forceinline__ float f(float a, float b) const { return a + b; }
 };
+struct GateOp {  // first operand: gate, second: attention output
+  __device__ __forceinline__ float f(float g, float a) const { return (1.0f / (1.0f + __expf(-g))) * a; }
+};
+
+// dst[r, :] = src[:]: one 16-byte chunk per thread per step, the source row
+// read through L1 (every CTA reads the same few KB), stores streamed.
+__global__ void __launch_bounds__(kThreads) broadcast_vec_kernel(uint4* dst, const uint4* src, int64_t n_copies,
+                                                                  int64_t chunks) {
+  const int64_t total = n_copies * chunks;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < total; i += stride)
+    st_stream(dst + i, ld_keep(src + i % chunks));
+}
+
+__global__ void __launch_bounds__(kThreads) broadcast_scalar_kernel(uint16_t* dst, const uint16_t* src,
+                                                                    int64_t n_copies, int64_t vec_len) {
+  const int64_t total = n_copies * vec_len;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < total; i += stride) dst[i] = src[i % vec_len];
+}
 
 template <class Op>
 __device__ __forceinline__ uint4 apply8(const Op& op, const uint4& a, const uint4& b) {
@@ -128,6 +150,28 @@ cudaError_t launch_swiglu(const void* gate, const void* up, void* out, int64_t n
 
 cudaError_t launch_additive_inject(const void* a, const void* b, void* out, int64_t n, cudaStream_t s) {
   return launch_ew<AddOp>(a, b, out, n, s);
+}
+
+cudaError_t launch_attn_gate(const void* gate, const void* attn, void* out, int64_t n, cudaStream_t s) {
+  return launch_ew<GateOp>(gate, attn, out, n, s);
+}
+
+cudaError_t launch_broadcast(void* dst, const void* src, int64_t n_copies, int64_t vec_len, cudaStream_t s) {
+  const int64_t cap = (int64_t)device_sm_count() * (2048 / kThreads) * 4;
+  if (vec_len % 8 == 0 && aligned16(dst) && aligned16(src)) {
+    const int64_t chunks = vec_len / 8;
+    int64_t blocks = (n_copies * chunks + kThreads - 1) / kThreads;
+    if (blocks > cap) blocks = cap;
+    broadcast_vec_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<uint4*>(dst),
+                                                               static_cast<const uint4*>(src), n_copies, chunks);
+  } else {
+    int64_t blocks = (n_copies * vec_len + kThreads - 1) / kThreads;
+    if (blocks > cap) blocks = cap;
+    broadcast_scalar_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<uint16_t*>(dst),
+                                                                  static_cast<const uint16_t*>(src), n_copies,
+                                                                  vec_len);
+  }
+  return cudaGetLastError();
 }
 
 }  // namespace hrm

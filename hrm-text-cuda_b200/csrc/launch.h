@@ -14,6 +14,8 @@ int device_sm_count();
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 cudaError_t launch_additive_inject(const void* a, const void* b, void* out, int64_t n, cudaStream_t s);
+cudaError_t launch_attn_gate(const void* gate, const void* attn, void* out, int64_t n, cudaStream_t s);
+cudaError_t launch_broadcast(void* dst, const void* src, int64_t n_copies, int64_t vec_len, cudaStream_t s);
 cudaError_t launch_swiglu(const void* gate, const void* up, void* out, int64_t n, cudaStream_t s);
 
 cudaError_t launch_rms_norm_bf16(const void* x, void* y, const void* w, int64_t rows, int64_t hidden,
@@ -35,5 +37,7 @@ cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, vo
                               float theta, const float* table, int64_t cache_len, int64_t cache_offset,
                               cudaStream_t s);
 cudaError_t launch_rope_table(float* table, int64_t max_pos, int64_t head_dim, float theta, cudaStream_t s);
+
+cudaError_t launch_convert_to_bf16(const void* src, int dtype, void* dst, int64_t n, cudaStream_t s);
 
 }  // namespace hrm

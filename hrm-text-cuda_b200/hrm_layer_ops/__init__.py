@@ -8,6 +8,10 @@ from ._lib import HrmError, LIB, LIB_PATH  # noqa: F401
 from .ops import (  # noqa: F401
     add_rms_norm,
     additive_inject,
+    apply_attn_gate,
+    broadcast_vec,
+    convert_to_bf16,
+    gated_attn_output,
     embed_rms_norm,
     embedding_lookup,
     rms_norm,
@@ -28,4 +32,8 @@ __all__ = [
     "embedding_lookup",
     "embed_rms_norm",
     "split_gqkv_rope",
+    "apply_attn_gate",
+    "gated_attn_output",
+    "broadcast_vec",
+    "convert_to_bf16",
 ]

@@ -19,6 +19,8 @@ HRM_ERR_INVALID_SHAPE = 2
 HRM_ERR_SIZE_OVERFLOW = 3
 HRM_ERR_ALIASING = 4
 HRM_ERR_TABLE_RANGE = 5
+HRM_ERR_DTYPE = 6
+DTYPES = {"bf16": 0, "f32": 1, "f16": 2}
 HRM_ERR_CUDA = 1000
 
 _p = ctypes.c_void_p
@@ -38,6 +40,10 @@ SIGNATURES = {
     "hrm_embed_rms_norm": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f32, _f32, _p],
     "hrm_split_gqkv_rope": [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _i64,
                             _i64, _p],
+    "hrm_apply_attn_gate": [_p, _p, _i64, _p],
+    "hrm_gated_attn_output": [_p, _p, _p, _i64, _p],
+    "hrm_broadcast_vec": [_p, _p, _i64, _i64, _p],
+    "hrm_convert_to_bf16": [_p, ctypes.c_int, _p, _i64, _p],
     "hrm_abi_version": [],
 }
 

@@ -229,3 +229,55 @@ def split_gqkv_rope(gqkv: torch.Tensor, num_heads: int, position_offset: int = 0
          num_heads, d, position_offset, theta, _ptr(table), positions, cache_len, cache_offset,
          _stream(gqkv, stream))
     return out
+
+
+def gated_attn_output(gate: torch.Tensor, attn_out: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+                      stream=None) -> torch.Tensor:
+    """out = sigmoid(gate) * attn_out (bf16).  src/lib.rs:505-527."""
+    _need(gate, "gate"); _need(attn_out, "attn_out")
+    if gate.numel() != attn_out.numel():
+        raise ValueError("gate and attn_out differ in size")
+    out = torch.empty_like(attn_out) if out is None else out
+    _need(out, "out")
+    call("hrm_gated_attn_output", _ptr(gate), _ptr(attn_out), _ptr(out), gate.numel(), _stream(gate, stream))
+    return out
+
+
+def apply_attn_gate(gate: torch.Tensor, attn_out: torch.Tensor, *, stream=None) -> torch.Tensor:
+    """attn_out *= sigmoid(gate), in place.  src/lib.rs:607-630."""
+    _need(gate, "gate"); _need(attn_out, "attn_out")
+    if gate.numel() != attn_out.numel():
+        raise ValueError("gate and attn_out differ in size")
+    call("hrm_apply_attn_gate", _ptr(gate), _ptr(attn_out), gate.numel(), _stream(gate, stream))
+    return attn_out
+
+
+def broadcast_vec(src: torch.Tensor, n_copies: int, out: Optional[torch.Tensor] = None, *,
+                  stream=None) -> torch.Tensor:
+    """out[r, :] = src for r < n_copies (bf16).  src/lib.rs:748-767."""
+    _need(src, "src")
+    out = torch.empty((n_copies, src.numel()), dtype=src.dtype, device=src.device) if out is None else out
+    _need(out, "out")
+    if out.numel() != n_copies * src.numel():
+        raise ValueError("out has the wrong size")
+    call("hrm_broadcast_vec", _ptr(out), _ptr(src), n_copies, src.numel(), _stream(src, stream))
+    return out
+
+
+def convert_to_bf16(raw: torch.Tensor, dtype: str, out: Optional[torch.Tensor] = None, *,
+                    stream=None) -> torch.Tensor:
+    """Checkpoint bytes (a CUDA uint8 tensor, any offset) of `dtype` ('f32', 'f16'
+    or 'bf16') -> bf16, as the reference's raw_to_bf16 (src/lib.rs:1981-2008)."""
+    from ._lib import DTYPES
+
+    _need(raw, "raw", (torch.uint8,))
+    size = 4 if dtype == "f32" else 2
+    if raw.numel() % size:
+        raise ValueError("raw byte count is not a multiple of the element size")
+    n = raw.numel() // size
+    out = torch.empty(n, dtype=torch.bfloat16, device=raw.device) if out is None else out
+    _need(out, "out")
+    if out.numel() != n:
+        raise ValueError("out has the wrong size")
+    call("hrm_convert_to_bf16", _ptr(raw), DTYPES[dtype], _ptr(out), n, _stream(raw, stream))
+    return out

@@ -40,6 +40,7 @@ enum hrm_status {
   HRM_ERR_SIZE_OVERFLOW = 3,  /* a product of sizes overflows int64 / grid limits */
   HRM_ERR_ALIASING = 4,       /* buffers that must be distinct overlap           */
   HRM_ERR_TABLE_RANGE = 5,    /* position_offset + seq_len exceeds the rope table */
+  HRM_ERR_DTYPE = 6,          /* unsupported element type                        */
   HRM_ERR_CUDA = 1000         /* HRM_ERR_CUDA + cudaError_t of the failed launch  */
 };
 
@@ -56,6 +57,24 @@ int hrm_abi_version(void);
  * z_out may alias z_a or z_b exactly (elementwise, in place is fine).      */
 int hrm_additive_inject(const void* z_a, const void* z_b, void* z_out,
                         int64_t total_elements, hrm_stream_t stream);
+
+/* Sigmoid-gated attention output:
+ *   out[i] = bf16_rn((1 / (1 + exp(-g))) * a),  g = f32(gate[i]), a = f32(attn[i])
+ * (exp by the __expf intrinsic, as in the reference).  hrm_apply_attn_gate
+ * writes in place over attn_out and replaces HrmForwardPass::apply_attn_gate
+ * (src/lib.rs:607-630, src/kernels/apply_attn_gate.cu:8-42);
+ * hrm_gated_attn_output writes to `output` (which may alias attn_out exactly)
+ * and replaces HrmForwardPass::gated_attn_output (src/lib.rs:505-527,
+ * src/kernels/gated_attn_output.cu:8-43).                                   */
+int hrm_apply_attn_gate(const void* gate, void* attn_out, int64_t total_elements, hrm_stream_t stream);
+int hrm_gated_attn_output(const void* gate, const void* attn_out, void* output, int64_t total_elements,
+                          hrm_stream_t stream);
+
+/* dst[r, j] = src[j] for r < n_copies, j < vec_len (bf16).  Replaces
+ * HrmForwardPass::broadcast_vec (src/lib.rs:748-767,
+ * src/kernels/broadcast_vec.cu:7-21), used to initialise z_L from z_l_init
+ * (src/lib.rs:1203).  dst must not overlap src.                             */
+int hrm_broadcast_vec(void* dst, const void* src, int64_t n_copies, int64_t vec_len, hrm_stream_t stream);
 
 /* RMSNorm over the last dim of a row-major [rows, hidden_size] bf16 tensor:
  *   ss  = sum_j f32(x_j)^2   (fp32, the reference's 256-thread order)
@@ -170,6 +189,19 @@ int hrm_split_gqkv_rope(const void* gqkv, void* gate_out, void* q_out, void* k_o
                         int64_t num_heads, int64_t head_dim, int64_t position_offset, float theta,
                         const float* rope_table, int64_t table_positions, int64_t cache_len,
                         int64_t cache_offset, hrm_stream_t stream);
+
+/* Element types of checkpoint tensors (safetensors dtypes). */
+enum hrm_dtype { HRM_DTYPE_BF16 = 0, HRM_DTYPE_F32 = 1, HRM_DTYPE_F16 = 2 };
+
+/* Converts n little-endian values of src_dtype at `src` (raw checkpoint
+ * bytes copied to the device, any byte alignment) to bf16 at `dst`, with the
+ * conversions of the reference's weight loader raw_to_bf16
+ * (src/lib.rs:1981-2008), i.e. half 2.7.1's bf16::from_f32 (round to nearest
+ * even; a NaN keeps its sign and top payload bits and gets the quiet bit) and
+ * f16::to_f32 (exact widening) before it.  BF16 is copied as is.  Replaces
+ * that host loop so a checkpoint can be uploaded raw and converted on the
+ * GPU.  dst must not overlap src.                                           */
+int hrm_convert_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, hrm_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -250,3 +250,55 @@ void ora_kv_cache_update(const uint16_t* k, const uint16_t* v, uint16_t* k_cache
     memcpy(v_cache + (bh * max_len + pos) * head_dim, v + r * head_dim, (size_t)head_dim * 2);
   }
 }
+
+/* apply_attn_gate.cu:28-29: sigmoid first, then times a, one rounding. */
+void ora_gated_attn_output(const uint16_t* gate, const uint16_t* attn, uint16_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    const float g = ora_bf16_to_f32(gate[i]), a = ora_bf16_to_f32(attn[i]);
+    out[i] = ora_f32_to_bf16((1.0f / (1.0f + expf(-g))) * a);
+  }
+}
+
+/* broadcast_vec.cu:102-105 */
+void ora_broadcast_vec(uint16_t* dst, const uint16_t* src, int64_t n_copies, int64_t vec_len) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < n_copies; ++r) memcpy(dst + r * vec_len, src, (size_t)vec_len * 2);
+}
+
+/* half 2.7.1 bf16::from_f32: a NaN keeps sign and high bits and is made
+ * quiet; otherwise round half to even on bit 15 (round bit) with the low 15
+ * bits and bit 16 (the kept LSB) deciding ties. */
+static uint16_t half_f32_to_bf16(uint32_t x) {
+  if ((x & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((x >> 16) | 0x0040u);
+  if ((x & 0x8000u) && (x & 0x17fffu)) return (uint16_t)((x >> 16) + 1u);
+  return (uint16_t)(x >> 16);
+}
+
+/* half 2.7.1 f16::to_f32: exact; NaN payload shifted up with the quiet bit. */
+static uint32_t half_f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const int exp = (h >> 10) & 0x1f;
+  const uint32_t man = h & 0x3ffu;
+  if (exp == 0x1f) return sign | (man ? 0x7fc00000u | (man << 13) : 0x7f800000u);
+  /* finite: the value is man * 2^(exp - 25) (+ implicit one), exact in fp32 */
+  const float mag = exp == 0 ? ldexpf((float)man, -24) : ldexpf((float)(man | 0x400u), exp - 25);
+  uint32_t bits;
+  memcpy(&bits, &mag, 4);
+  return sign | bits;
+}
+
+void ora_convert_to_bf16(const void* src, int dtype, uint16_t* dst, int64_t n) {
+  const uint8_t* b = (const uint8_t*)src;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    if (dtype == 1) {
+      const uint32_t x = (uint32_t)b[4 * i] | (uint32_t)b[4 * i + 1] << 8 | (uint32_t)b[4 * i + 2] << 16 |
+                         (uint32_t)b[4 * i + 3] << 24;
+      dst[i] = half_f32_to_bf16(x);
+    } else {
+      const uint16_t h = (uint16_t)(b[2 * i] | b[2 * i + 1] << 8);
+      dst[i] = dtype == 2 ? half_f32_to_bf16(half_f16_to_f32(h)) : h;
+    }
+  }
+}

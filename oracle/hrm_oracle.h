@@ -58,6 +58,19 @@ void ora_rope_table(float* table, int64_t positions, int64_t head_dim, float the
 void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                     int64_t offset, float theta, const float* table);
 
+/* apply_attn_gate.cu:28-29 / gated_attn_output.cu:71-72:
+ * out = (1 / (1 + exp(-g))) * a (expf in place of the __expf intrinsic). */
+void ora_gated_attn_output(const uint16_t* gate, const uint16_t* attn, uint16_t* out, int64_t n);
+
+/* broadcast_vec.cu:102-105: dst[r, j] = src[j]. */
+void ora_broadcast_vec(uint16_t* dst, const uint16_t* src, int64_t n_copies, int64_t vec_len);
+
+/* The reference's weight loader raw_to_bf16 (src/lib.rs:1981-2008) with the
+ * half 2.7.1 conversions it calls (Cargo.lock: half 2.7.1, not vendored;
+ * restated from its documented behaviour): dtype 0 bf16 copy, 1 f32, 2 f16;
+ * src is little-endian bytes. */
+void ora_convert_to_bf16(const void* src, int dtype, uint16_t* dst, int64_t n);
+
 /* split_gqkv.cu:27-48: per token [gate | q | k | v] heads -> gate [b, s, h, :],
  * q, k, v [b, h, s, :] (plain copies). */
 void ora_split_gqkv(const uint16_t* gqkv, uint16_t* gate, uint16_t* q, uint16_t* k, uint16_t* v, int64_t batch,

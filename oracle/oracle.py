@@ -81,6 +81,9 @@ class Oracle:
         "ora_rope_embed": [_p, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p],
         "ora_split_gqkv": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64],
         "ora_kv_cache_update": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int],
+        "ora_gated_attn_output": [_p, _p, _p, _i64],
+        "ora_broadcast_vec": [_p, _p, _i64, _i64],
+        "ora_convert_to_bf16": [_p, ctypes.c_int, _p, _i64],
         "ora_set_threads": [ctypes.c_int],
     }
 
@@ -172,6 +175,29 @@ class Oracle:
         return q, k
 
 
+    def gated_attn_output(self, gate, attn):
+        gate, attn = self._c(gate, np.uint16), self._c(attn, np.uint16)
+        out = np.empty_like(attn)
+        self.lib.ora_gated_attn_output(self._ptr(gate), self._ptr(attn), self._ptr(out), attn.size)
+        return out
+
+    def broadcast_vec(self, src, n_copies):
+        src = self._c(src, np.uint16)
+        out = np.empty((n_copies, src.size), np.uint16)
+        self.lib.ora_broadcast_vec(self._ptr(out), self._ptr(src), n_copies, src.size)
+        return out
+
+    DTYPES = {"bf16": 0, "f32": 1, "f16": 2}
+
+    def convert_to_bf16(self, raw: bytes, dtype: str):
+        """raw little-endian bytes of a checkpoint tensor -> bf16 bits."""
+        size = 4 if dtype == "f32" else 2
+        buf = np.frombuffer(raw, np.uint8)
+        n = buf.size // size
+        out = np.empty(n, np.uint16)
+        self.lib.ora_convert_to_bf16(buf.ctypes.data_as(_p), self.DTYPES[dtype], self._ptr(out), n)
+        return out
+
     def split_gqkv(self, gqkv, batch, seq, heads, head_dim):
         gqkv = self._c(gqkv, np.uint16)
         gate = np.empty((batch, seq, heads, head_dim), np.uint16)
@@ -213,6 +239,9 @@ class RefKernels:
         "ref_embedding_lookup": [_p, _p, _p, _i64, _i64, _i64, _i64, _f32, _p],
         "ref_split_gqkv": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
         "ref_kv_cache_update": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _p],
+        "ref_apply_attn_gate": [_p, _p, _i64, _p],
+        "ref_gated_attn_output": [_p, _p, _p, _i64, _p],
+        "ref_broadcast_vec": [_p, _p, _i64, _i64, _p],
     }
 
     def __init__(self, path: str = REF_LIB):
@@ -263,3 +292,13 @@ class RefKernels:
         b, h, s, d = k.shape
         self._run("ref_kv_cache_update", _p(k.data_ptr()), _p(v.data_ptr()), _p(k_cache.data_ptr()),
                   _p(v_cache.data_ptr()), b, h, s, d, k_cache.shape[2], cached_len, int(is_decode))
+
+    def apply_attn_gate(self, gate, attn):
+        self._run("ref_apply_attn_gate", _p(gate.data_ptr()), _p(attn.data_ptr()), attn.numel())
+
+    def gated_attn_output(self, gate, attn, out):
+        self._run("ref_gated_attn_output", _p(gate.data_ptr()), _p(attn.data_ptr()), _p(out.data_ptr()),
+                  attn.numel())
+
+    def broadcast_vec(self, dst, src):
+        self._run("ref_broadcast_vec", _p(dst.data_ptr()), _p(src.data_ptr()), dst.shape[0], src.numel())

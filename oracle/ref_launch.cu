@@ -9,7 +9,10 @@
 #include <stdint.h>
 
 #include "additive_inject.cu"
+#include "apply_attn_gate.cu"
+#include "broadcast_vec.cu"
 #include "embedding_lookup.cu"
+#include "gated_attn_output.cu"
 #include "kv_cache_update.cu"
 #include "rms_norm.cu"
 #include "rope_embed.cu"
@@ -83,6 +86,30 @@ int ref_kv_cache_update(const void* k, const void* v, void* kc, void* vc, int64_
                                                           (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, (int)batch,
                                                           (int)heads, (int)seq, (int)head_dim, (int)max_len,
                                                           (int)cached_len, is_decode);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:613-627 (in place)
+int ref_apply_attn_gate(const void* gate, void* attn, int64_t n, cudaStream_t s) {
+  apply_attn_gate_kernel<<<blocks_for((n + 7) / 8, 256), 256, 0, s>>>((const __nv_bfloat16*)gate,
+                                                                      (__nv_bfloat16*)attn, (int)n);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:512-524
+int ref_gated_attn_output(const void* gate, const void* attn, void* out, int64_t n, cudaStream_t s) {
+  gated_attn_output_kernel<<<blocks_for((n + 7) / 8, 256), 256, 0, s>>>(
+      (const __nv_bfloat16*)gate, (const __nv_bfloat16*)attn, (__nv_bfloat16*)out, (int)n);
+  return (int)cudaGetLastError();
+}
+
+// src/lib.rs:755-764
+int ref_broadcast_vec(void* dst, const void* src, int64_t n_copies, int64_t vec_len, cudaStream_t s) {
+  int64_t blocks = (n_copies * vec_len + 255) / 256;
+  if (blocks > 65535) blocks = 65535;
+  if (blocks < 1) blocks = 1;
+  broadcast_vec_kernel<<<(unsigned)blocks, 256, 0, s>>>((__nv_bfloat16*)dst, (const __nv_bfloat16*)src,
+                                                        (int)n_copies, (int)vec_len);
   return (int)cudaGetLastError();
 }
 

@@ -38,6 +38,9 @@ KATS = {
         # src/lib.rs:2265-2279
         "swiglu_ffn": {"gate": [0.0, 0.0, 0.0, 0.0], "up": [2.0, 2.0, 2.0, 2.0],
                        "expected": [0.0, 0.0, 0.0, 0.0]},
+        # src/lib.rs:2283-2298
+        "gated_attn_output": {"gate": [0.0, 0.0, 0.0, 0.0], "attn": [1.0, 1.0, 1.0, 1.0],
+                              "expected": [0.5, 0.5, 0.5, 0.5]},
     },
 }
 

@@ -180,3 +180,44 @@ def test_oracle_matches_reference_kernels(oracle, path):
             err = ulp_error(got, want, rope_pair_magnitude(want))
             assert err.max() <= ULP_TOL, f"rope max {err.max()} ulp"
 
+
+
+def test_reference_kat_gated_attn_output(oracle):
+    k = load_kats()
+    t = k["tests"]["gated_attn_output"]
+    y = bf16_to_f32(oracle.gated_attn_output(f32_to_bf16(np.array(t["gate"], np.float32)),
+                                             f32_to_bf16(np.array(t["attn"], np.float32))))
+    assert np.all(np.abs(y - np.array(t["expected"])) < k["tolerance"])
+
+
+def test_broadcast_vec(oracle, rng):
+    src = normal_bf16(rng, 37)
+    out = oracle.broadcast_vec(src, 5)
+    assert out.shape == (5, 37) and all(np.array_equal(r, src) for r in out)
+
+
+def test_convert_f16_exhaustive_matches_exact_widening(oracle):
+    """Every f16 pattern: finite and infinite values equal numpy's exact f16 -> f32
+    widening rounded to nearest even; NaNs keep sign and payload top bits, quiet."""
+    h = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    got = oracle.convert_to_bf16(h.tobytes(), "f16")
+    f = h.view(np.float16).astype(np.float32)
+    num = ~np.isnan(f)
+    assert np.array_equal(got[num], f32_to_bf16(f[num]))
+    nan = np.flatnonzero(~num)
+    want = ((h[nan].astype(np.uint32) & 0x8000) | 0x7FC0 | ((h[nan].astype(np.uint32) & 0x3FF) >> 3)).astype(np.uint16)
+    assert np.array_equal(got[nan], want)
+
+
+def test_convert_f32_rounding_and_nan_rule(oracle, rng):
+    x = rng.standard_normal(100000).astype(np.float32) * np.float32(1e3)
+    specials = np.array([0x00000000, 0x80000000, 0x7F800000, 0xFF800000, 0x00000001, 0x807FFFFF,
+                         0x3F808000, 0x3F818000, 0x3F808001, 0x7F7FFFFF, 0x7F7F8000, 0x7F7F7FFF],
+                        np.uint32).view(np.float32)
+    x = np.concatenate([x, specials])
+    assert np.array_equal(oracle.convert_to_bf16(x.tobytes(), "f32"), f32_to_bf16(x))
+    nans = np.array([0x7FC00000, 0xFFC00001, 0x7F800001, 0xFFA5A5A5, 0x7FFFFFFF], np.uint32)
+    got = oracle.convert_to_bf16(nans.tobytes(), "f32")
+    assert np.array_equal(got, ((nans >> 16) | 0x40).astype(np.uint16))
+    raw = normal_bf16(rng, 1000)
+    assert np.array_equal(oracle.convert_to_bf16(raw.tobytes(), "bf16"), raw)

@@ -270,3 +270,55 @@ def test_split_gqkv_rope_errors(cuda):
         ops.split_gqkv_rope(g, 2, 3, 10000.0, None, kc, kc.clone(), cache_offset=3)
     with pytest.raises(ValueError):
         ops.split_gqkv_rope(g, 2, 0, 10000.0, None, kc, None)
+
+
+# ----------------------------------------- attention gate, broadcast, convert
+@pytest.mark.parametrize("n", [1, 4, 9, 4099, 65536 * 3 + 5])
+def test_gated_attn_output_and_in_place(oracle, rng, cuda, n):
+    g, a = normal_bf16(rng, n, 2.0), normal_bf16(rng, n)
+    want = oracle.gated_attn_output(g, a)
+    out = to_host(ops.gated_attn_output(to_dev(g, cuda), to_dev(a, cuda)))
+    assert ulp_error(out, want).max() <= ULP_TOL
+    da = to_dev(a, cuda)
+    ops.apply_attn_gate(to_dev(g, cuda), da)
+    assert_bits_equal(to_host(da), out, "in place == out of place")
+
+
+def test_gated_attn_output_reference_kat(cuda):
+    """src/lib.rs:2283-2298: sigmoid(0) * 1 = 0.5."""
+    y = ops.gated_attn_output(torch.zeros(4, dtype=torch.bfloat16, device=cuda),
+                              torch.ones(4, dtype=torch.bfloat16, device=cuda)).float().cpu().numpy()
+    assert np.all(np.abs(y - 0.5) < 0.01)
+
+
+@pytest.mark.parametrize("n_copies,vec_len", [(1, 8), (7, 2048), (64, 1536), (5, 13), (3000, 2048)])
+def test_broadcast_vec(oracle, rng, cuda, n_copies, vec_len):
+    src = normal_bf16(rng, vec_len)
+    assert_bits_equal(to_host(ops.broadcast_vec(to_dev(src, cuda), n_copies)), oracle.broadcast_vec(src, n_copies),
+                      "broadcast")
+
+
+def _raw(b: bytes, cuda, offset=0):
+    buf = torch.zeros(len(b) + offset, dtype=torch.uint8, device=cuda)
+    buf[offset:] = torch.frombuffer(bytearray(b), dtype=torch.uint8).to(cuda)
+    return buf[offset:]
+
+
+def test_convert_f16_exhaustive(oracle, cuda):
+    h = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    want = oracle.convert_to_bf16(h.tobytes(), "f16")
+    for off in (0, 1, 2, 6):  # vector path (0) and byte-assembled paths
+        got = to_host(ops.convert_to_bf16(_raw(h.tobytes(), cuda, off), "f16"))
+        assert_bits_equal(got, want, f"f16 offset {off}")
+
+
+def test_convert_f32(oracle, rng, cuda):
+    x = np.concatenate([rng.standard_normal(1 << 20).astype(np.float32) * np.float32(1e3),
+                        np.array([0x7FC00000, 0xFFC00001, 0x7F800001, 0xFFA5A5A5, 0x7FFFFFFF, 0x00000001, 0x3F808000,
+                                  0x3F818000, 0x7F7FFFFF, 0x80000000, 0x7F800000], np.uint32).view(np.float32)])
+    want = oracle.convert_to_bf16(x.tobytes(), "f32")
+    for off in (0, 3):
+        got = to_host(ops.convert_to_bf16(_raw(x.tobytes(), cuda, off), "f32"))
+        assert_bits_equal(got, want, f"f32 offset {off}")
+    b = normal_bf16(rng, 1001)
+    assert_bits_equal(to_host(ops.convert_to_bf16(_raw(b.tobytes(), cuda), "bf16")), b, "bf16 copy")

@@ -157,6 +157,16 @@ def test_throughput_vs_reference_kernels(ref, cuda):
         nb / _time(lambda: (ref.split_gqkv(gq, gate, qq, kk, vv), ref.rope_embed(qq, kk, 0, 10000.0),
                             ref.kv_cache_update(kk, vv, kc, vc, 0, False))))
     del gq, gate, qq, kk, vv, kc, vc
+    # attention gate in place [65536 x 2048] (the reference's apply_attn_gate)
+    ga, at = rn((65536, 2048)), rn((65536, 2048))
+    nb = ga.numel() * 6
+    res["apply_attn_gate"] = (nb / _time(lambda: ops.apply_attn_gate(ga, at)), nb / _time(lambda: ref.apply_attn_gate(ga, at)))
+    # broadcast z_l_init to 65536 rows of 2048
+    zl = rn(2048)
+    zo = torch.empty((65536, 2048), dtype=bf, device=cuda)
+    nb = zo.numel() * 2
+    res["broadcast_vec"] = (nb / _time(lambda: ops.broadcast_vec(zl, 65536, out=zo)), nb / _time(lambda: ref.broadcast_vec(zo, zl)))
+    del ga, at, zo
     # SwiGLU [32768 x 5632]
     gg, uu = rn((32768, 5632), 0.5), rn((32768, 5632), 0.5)
     oo = torch.empty_like(gg)
@@ -200,3 +210,19 @@ def test_split_gqkv_rope_matches_reference_sequence(ref, rng, cuda, b, s, h, d, 
     outs = ops.split_gqkv_rope(gqkv, h, off, 10000.0, table, mkc, mvc, cache_offset=off)
     for got, want, name in zip((*outs, mkc, mvc), (rg, rq, rk, rv, rkc, rvc), ("gate", "q", "k", "v", "kc", "vc")):
         assert_bits_equal(to_host(got), to_host(want), name)
+
+
+def test_attn_gate_and_broadcast_match_reference(ref, rng, cuda):
+    g, a = to_dev(normal_bf16(rng, 300007, 2.0), cuda), to_dev(normal_bf16(rng, 300007), cuda)
+    g[:4] = torch.tensor([0.0, float("inf"), float("-inf"), float("nan")], dtype=torch.bfloat16)
+    r1, r2 = torch.empty_like(a), a.clone()
+    ref.gated_attn_output(g, a, r1)
+    ref.apply_attn_gate(g, r2)
+    assert_bits_equal(to_host(ops.gated_attn_output(g, a)), to_host(r1), "gated_attn_output")
+    m = a.clone()
+    ops.apply_attn_gate(g, m)
+    assert_bits_equal(to_host(m), to_host(r2), "apply_attn_gate")
+    src = to_dev(normal_bf16(rng, 1536), cuda)
+    rb = torch.empty((1000, 1536), dtype=torch.bfloat16, device=cuda)
+    ref.broadcast_vec(rb, src)
+    assert_bits_equal(to_host(ops.broadcast_vec(src, 1000)), to_host(rb), "broadcast_vec")
