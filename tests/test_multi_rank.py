@@ -102,3 +102,38 @@ def test_gloo_world2_sharded_equals_unsharded():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = q.get(timeout=5)
     assert res == dict(y_ok=True, r_ok=True, q_ok=True, t_max=2.0, sums_ok=True), res
+
+
+def _dying_worker(rank, world, port, result_q):
+    """Rank 1 raises before the collective; rank 0 must get an error, not hang."""
+    import datetime
+    import time
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)  # a rank that dies between steps, with nothing in flight
+    t0 = time.time()
+    try:
+        t = torch.ones(1)
+        dist.all_reduce(t)
+        result_q.put(("no error", time.time() - t0))
+    except Exception as e:  # noqa: BLE001 - any error is the detection we want
+        result_q.put((type(e).__name__, time.time() - t0))
+    result_q.close()
+    result_q.join_thread()  # flush before the hard exit
+    os._exit(0)
+
+
+def test_gloo_dead_rank_is_detected_within_timeout():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    assert procs[1].exitcode == 3
+    kind, waited = q.get(timeout=5)
+    assert kind != "no error" and waited < 60, (kind, waited)
