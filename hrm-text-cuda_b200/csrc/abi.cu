@@ -157,9 +157,13 @@ int hrm_add_rms_norm(const void* x, const void* branch, void* residual_out, void
       hrm::launch_add_rms_norm(x, branch, residual_out, normed_out, weight, rows, hidden_size, eps, as_cuda(stream)));
 }
 
-int hrm_rope_embed(void* q, void* k, int64_t batch_size, int64_t num_heads, int64_t seq_len, int64_t head_dim,
-                   int64_t position_offset, float theta, const float* rope_table, int64_t table_positions,
-                   hrm_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+int rope_common(void* q, void* k, int64_t batch_size, int64_t num_heads, int64_t seq_len, int64_t head_dim,
+                int64_t position_offset, float theta, const float* rope_table, int64_t table_positions,
+                bool token_major, hrm_stream_t stream) {
   if (batch_size < 0 || num_heads < 0 || seq_len < 0 || head_dim <= 0 || head_dim % 2 != 0 ||
       position_offset < 0 || num_heads > INT32_MAX || head_dim > INT32_MAX)
     return HRM_ERR_INVALID_SHAPE;
@@ -176,7 +180,25 @@ int hrm_rope_embed(void* q, void* k, int64_t batch_size, int64_t num_heads, int6
     if (overlap(rope_table, tbytes, q, bytes) || overlap(rope_table, tbytes, k, bytes)) return HRM_ERR_ALIASING;
   }
   return cuda_status(hrm::launch_rope(q, k, batch_size, num_heads, seq_len, head_dim, position_offset, theta,
-                                      rope_table, as_cuda(stream)));
+                                      rope_table, token_major, as_cuda(stream)));
+}
+
+}  // namespace
+
+extern "C" {
+
+int hrm_rope_embed(void* q, void* k, int64_t batch_size, int64_t num_heads, int64_t seq_len, int64_t head_dim,
+                   int64_t position_offset, float theta, const float* rope_table, int64_t table_positions,
+                   hrm_stream_t stream) {
+  return rope_common(q, k, batch_size, num_heads, seq_len, head_dim, position_offset, theta, rope_table,
+                     table_positions, false, stream);
+}
+
+int hrm_rope_embed_token_major(void* q, void* k, int64_t batch_size, int64_t seq_len, int64_t num_heads,
+                               int64_t head_dim, int64_t position_offset, float theta, const float* rope_table,
+                               int64_t table_positions, hrm_stream_t stream) {
+  return rope_common(q, k, batch_size, num_heads, seq_len, head_dim, position_offset, theta, rope_table,
+                     table_positions, true, stream);
 }
 
 int hrm_rope_table_build(float* table, int64_t max_positions, int64_t head_dim, float theta, hrm_stream_t stream) {

@@ -31,7 +31,7 @@ cudaError_t launch_embedding(const uint32_t* ids, const void* table, void* out, 
                              int64_t vocab, float scale, cudaStream_t s);
 
 cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
-                        int64_t offset, float theta, const float* table, cudaStream_t s);
+                        int64_t offset, float theta, const float* table, bool token_major, cudaStream_t s);
 cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, void* v, void* kc, void* vc,
                               int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t offset,
                               float theta, const float* table, int64_t cache_len, int64_t cache_offset,

@@ -1,5 +1,6 @@
 // Rotary position embedding, in place on Q and K ([batch, heads, seq, head_dim]
-// bf16), rotate-half pairing (x[i], x[i + head_dim/2]) as in
+// bf16 as the reference lays them out, or token-major [batch, seq, heads,
+// head_dim]), rotate-half pairing (x[i], x[i + head_dim/2]) as in
 // src/kernels/rope_embed.cu:36-53.
 //
 // Fast path (head_dim % 16 == 0, head_dim <= 512, 16-byte aligned): a thread
@@ -54,6 +55,9 @@ constexpr int kHeadUnroll = HRM_ROPE_UNROLL;
 struct RopeArgs {
   uint4* q;
   uint4* k;
+  // 16-byte-chunk strides of a (batch, position, head) row start:
+  // [b, h, s, d]: heads * seq * rc, rc, seq * rc; [b, s, h, d]: seq * heads * rc, heads * rc, rc
+  int64_t batch_stride, pos_stride, head_stride;
   const float4* table;  // [positions][head_dim] floats: cos in [0, hd/2), sin in [hd/2, hd)
   int64_t seq;
   int64_t tiles_per_batch;
@@ -120,7 +124,6 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel
   const int rest = threadIdx.x / a.g;
   const int slice = rest % a.ht;
   const int pl = rest / a.ht;
-  const int row_chunks = 2 * a.g;
 
   for (int64_t tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
     const int64_t b = tile / a.tiles_per_batch;
@@ -131,9 +134,8 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel
     float c[8], sn[8];
     load_cos_sin<TABLE>(a.table, pos, j, a.head_dim, a.theta, c, sn);
 
-    // Chunk index of (b, h, s) row start: ((b * heads + h) * seq + s) * row_chunks.
-    const int64_t head_step = a.seq * row_chunks;
-    const int64_t row0 = ((b * a.heads) * a.seq + s) * row_chunks + j;
+    const int64_t head_step = a.head_stride;
+    const int64_t row0 = b * a.batch_stride + s * a.pos_stride + j;
     int h = slice;
     for (; h + (kHeadUnroll - 1) * a.ht < a.heads; h += kHeadUnroll * a.ht) {
       uint4 ql[kHeadUnroll], qh[kHeadUnroll], kl[kHeadUnroll], kh[kHeadUnroll];
@@ -172,16 +174,18 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel
 
 // Any even head_dim / alignment: one thread per pair, as the reference maps
 // its threads (src/kernels/rope_embed.cu:22-37), with 64-bit indexing.
+// Rows enumerate (b, h, s) for [b, h, s, d] (heads_inner = 1) or (b, s, h)
+// for [b, s, h, d] (heads_inner = heads).
 __global__ void __launch_bounds__(256) rope_scalar_kernel(uint16_t* q, uint16_t* k, int64_t rows, int64_t seq,
-                                                          int head_dim, int offset, float theta,
-                                                          const float* table) {
+                                                          int64_t heads_inner, int head_dim, int offset,
+                                                          float theta, const float* table) {
   const int half = head_dim / 2;
   const int64_t total = rows * half;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
     const int i = (int)(idx % half);
     const int64_t row = idx / half;
-    const int pos = (int)(row % seq) + offset;
+    const int pos = (int)((row / heads_inner) % seq) + offset;
     float c, s;
     if (table != nullptr) {
       c = table[(int64_t)pos * head_dim + i];
@@ -352,7 +356,7 @@ int pow2_ceil(int64_t x) {
 }  // namespace
 
 cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
-                        int64_t offset, float theta, const float* table, cudaStream_t s) {
+                        int64_t offset, float theta, const float* table, bool token_major, cudaStream_t s) {
   const int64_t sms = device_sm_count();
   const int g = (int)(head_dim / 16);
   const bool fast = head_dim % 16 == 0 && head_dim <= 512 && (g & (g - 1)) == 0 && aligned16(q) &&
@@ -361,6 +365,10 @@ cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t 
     RopeArgs a;
     a.q = static_cast<uint4*>(q);
     a.k = static_cast<uint4*>(k);
+    const int64_t rc = 2 * g;
+    a.batch_stride = heads * seq * rc;
+    a.pos_stride = token_major ? heads * rc : rc;
+    a.head_stride = token_major ? rc : seq * rc;
     a.table = reinterpret_cast<const float4*>(table);
     a.seq = seq;
     a.heads = (int)heads;
@@ -385,7 +393,8 @@ cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t 
     int64_t blocks = (rows * (head_dim / 2) + 255) / 256;
     if (blocks > sms * 8) blocks = sms * 8;
     rope_scalar_kernel<<<(unsigned)blocks, 256, 0, s>>>(static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), rows,
-                                                        seq, (int)head_dim, (int)offset, theta, table);
+                                                        seq, token_major ? heads : 1, (int)head_dim, (int)offset,
+                                                        theta, table);
   }
   return cudaGetLastError();
 }

@@ -16,6 +16,7 @@ from .ops import (  # noqa: F401
     embedding_lookup,
     rms_norm,
     rope_embed,
+    rope_embed_token_major,
     rope_table,
     split_gqkv_rope,
     swiglu_ffn,
@@ -29,6 +30,7 @@ __all__ = [
     "add_rms_norm",
     "rope_table",
     "rope_embed",
+    "rope_embed_token_major",
     "embedding_lookup",
     "embed_rms_norm",
     "split_gqkv_rope",

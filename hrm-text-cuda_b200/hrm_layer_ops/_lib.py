@@ -34,6 +34,7 @@ SIGNATURES = {
     "hrm_rms_norm_f32": [_p, _p, _p, _i64, _i64, _f32, _p],
     "hrm_add_rms_norm": [_p, _p, _p, _p, _p, _i64, _i64, _f32, _p],
     "hrm_rope_embed": [_p, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _p],
+    "hrm_rope_embed_token_major": [_p, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _p],
     "hrm_rope_table_build": [_p, _i64, _i64, _f32, _p],
     "hrm_swiglu_ffn": [_p, _p, _p, _i64, _p],
     "hrm_embedding_lookup": [_p, _p, _p, _i64, _i64, _i64, _i64, _f32, _p],

@@ -152,6 +152,24 @@ def rope_embed(q: torch.Tensor, k: torch.Tensor, position_offset: int = 0, theta
     return q, k
 
 
+def rope_embed_token_major(q: torch.Tensor, k: torch.Tensor, position_offset: int = 0, theta: float = 10000.0,
+                           table: Optional[torch.Tensor] = None, *, stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """In-place RoPE on token-major q, k of shape [batch, seq, heads, head_dim]."""
+    _need(q, "q"); _need(k, "k")
+    if q.dim() != 4 or q.shape != k.shape:
+        raise ValueError("q and k must both be [batch, seq, heads, head_dim]")
+    b, s, h, d = q.shape
+    positions = 0
+    if table is not None:
+        _need(table, "table", (torch.float32,))
+        if table.dim() != 2 or table.shape[1] != d:
+            raise ValueError("table must be [positions, head_dim]")
+        positions = table.shape[0]
+    call("hrm_rope_embed_token_major", _ptr(q), _ptr(k), b, s, h, d, position_offset, theta, _ptr(table),
+         positions, _stream(q, stream))
+    return q, k
+
+
 def embedding_lookup(ids: torch.Tensor, table: torch.Tensor, embedding_scale: float,
                      out: Optional[torch.Tensor] = None, *, stream=None) -> torch.Tensor:
     """out[..., :] = table[clamp(ids)] * scale (bit-exact).  src/lib.rs:529-565."""

@@ -124,6 +124,16 @@ int hrm_rope_embed(void* q, void* k, int64_t batch_size, int64_t num_heads,
                    float theta, const float* rope_table,
                    int64_t table_positions, hrm_stream_t stream);
 
+/* The same rotation for token-major q and k, [batch, seq, heads, head_dim]
+ * (each token's heads contiguous, as a projection GEMM writes them); position
+ * of token s is s + position_offset.  No reference counterpart (the reference
+ * splits into [batch, heads, seq, head_dim] first); same arguments and rules
+ * as hrm_rope_embed, note the (batch, seq, heads) order.                    */
+int hrm_rope_embed_token_major(void* q, void* k, int64_t batch_size, int64_t seq_len,
+                               int64_t num_heads, int64_t head_dim, int64_t position_offset,
+                               float theta, const float* rope_table,
+                               int64_t table_positions, hrm_stream_t stream);
+
 /* Writes the fp32 cos/sin table used by hrm_rope_embed:
  *   table[p * head_dim + i]            = cos(a(p, i)),
  *   table[p * head_dim + head_dim/2 + i] = sin(a(p, i)),  p < max_positions,

@@ -64,3 +64,11 @@ def rope_pair_magnitude(bits):
     h = v.shape[-1] // 2
     m = np.maximum(v[..., :h], v[..., h:])
     return np.concatenate([m, m], axis=-1)
+
+
+def max_ulp(got_bits, want_bits, magnitude=None):
+    """Largest ulp error (see oracle.ulp_error); 0 for empty outputs."""
+    from oracle import ulp_error
+
+    err = ulp_error(got_bits, want_bits, magnitude)
+    return float(err.max()) if err.size else 0.0

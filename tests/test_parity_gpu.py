@@ -322,3 +322,19 @@ def test_convert_f32(oracle, rng, cuda):
         assert_bits_equal(got, want, f"f32 offset {off}")
     b = normal_bf16(rng, 1001)
     assert_bits_equal(to_host(ops.convert_to_bf16(_raw(b.tobytes(), cuda), "bf16")), b, "bf16 copy")
+
+
+@pytest.mark.parametrize("b,s,h,d,off", [(2, 300, 4, 128, 0), (64, 1, 16, 128, 4095), (1, 9, 3, 64, 5),
+                                         (1, 5, 2, 96, 1), (1, 4, 2, 130, 0)])
+@pytest.mark.parametrize("use_table", [False, True])
+def test_rope_token_major_equals_head_major(rng, cuda, b, s, h, d, off, use_table):
+    """[b, s, h, d] rotation == the [b, h, s, d] rotation of the transposed tensors, bit for bit."""
+    q, k = normal_bf16(rng, (b, s, h, d)), normal_bf16(rng, (b, s, h, d))
+    table = ops.rope_table(off + s, d) if use_table else None
+    tq, tk = to_dev(q, cuda), to_dev(k, cuda)
+    ops.rope_embed_token_major(tq, tk, off, 10000.0, table)
+    hq = to_dev(np.ascontiguousarray(q.transpose(0, 2, 1, 3)), cuda)
+    hk = to_dev(np.ascontiguousarray(k.transpose(0, 2, 1, 3)), cuda)
+    ops.rope_embed(hq, hk, off, 10000.0, table)
+    assert_bits_equal(to_host(tq), to_host(hq).transpose(0, 2, 1, 3), "q")
+    assert_bits_equal(to_host(tk), to_host(hk).transpose(0, 2, 1, 3), "k")
