@@ -7,7 +7,9 @@
 
 Default workload ("chain"): the chained layer-op pass on 65536 tokens per GPU
 -- embedding [32000 x 2048] ~ N(0, 0.02) gathered for ids ~ U[0, 32000) and
-RMSNorm'd (fused), RoPE on Q/K [16, 16, 4096, 128] with a fp32 cos/sin table,
+RMSNorm'd (fused), RoPE on token-major Q/K [16, 4096, 16, 128] (tokens x 16
+heads x 128; --qk-layout head for the reference's [B, 16, S, 128]) with a fp32
+cos/sin table,
 residual add + RMSNorm [65536 x 2048], SwiGLU [65536 x 5632] ~ 0.5 N(0, 1);
 norm weights 1 + 0.1 N(0, 1), eps 1e-5, scale sqrt(2048), theta 1e4.  Inputs
 are synthetic (seeded), generated on the device.  A step is one pass over
@@ -49,7 +51,7 @@ L2_BYTES = 126 * 1000 * 1000
 
 # chain shape (per GPU)
 HIDDEN, HEADS, HEAD_DIM, INTER, VOCAB = 2048, 16, 128, 5632, 32000
-CHAIN_B, CHAIN_S = 16, 4096               # Q/K [16, 16, 4096, 128] -> 65536 tokens
+CHAIN_B, CHAIN_S = 16, 4096               # 16 sequences of 4096 tokens = 65536 tokens
 DECODE_B = 64                             # decode shape: 64 tokens, seq 1, offset 4095
 EPS, THETA = 1e-5, 10000.0
 SCALE = 45.254833995939045                # (float)sqrt(2048)
@@ -66,6 +68,9 @@ def parse_args():
                              "attn_gate", "convert_f32"])
     ap.add_argument("--tokens", type=int, default=CHAIN_B * CHAIN_S,
                     help="chain tokens per GPU (a multiple of 4096; default 65536)")
+    ap.add_argument("--qk-layout", choices=["token", "head"], default="token",
+                    help="chain Q/K layout: token-major [B, S, 16, 128] or head-major [B, 16, S, 128]")
+    ap.add_argument("--chunk-tokens", type=int, default=4096, help="e2e pipeline chunk (token-major Q/K)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-oracle baseline leg")
     return ap.parse_args()
@@ -165,7 +170,7 @@ class Chain:
     name = "chain"
     dominant = "swiglu_ffn"
 
-    def __init__(self, device, rank, tokens=CHAIN_B * CHAIN_S):
+    def __init__(self, device, rank, tokens=CHAIN_B * CHAIN_S, token_major=True, chunk_tokens=4096):
         import torch
 
         from hrm_layer_ops import chain, ops
@@ -174,6 +179,7 @@ class Chain:
             raise SystemExit(f"--tokens must be a positive multiple of {CHAIN_S}")
         self.torch, self.chain, self.ops, self.device = torch, chain, ops, device
         self.batch = tokens // CHAIN_S
+        self.token_major, self.chunk_tokens = token_major, chunk_tokens
         T = tokens
         self.tokens = T
         wgen = torch.Generator(device=device).manual_seed(1234)          # weights: same on every rank
@@ -183,8 +189,9 @@ class Chain:
             w2=randn_bf16(HIDDEN, wgen, device, 0.1, 1.0), rope=ops.rope_table(CHAIN_S, HEAD_DIM, THETA, device),
             scale=SCALE, eps=EPS, theta=THETA)
         self.ids = torch.randint(0, VOCAB, (T,), generator=gen, device=device, dtype=torch.int32)
-        self.q = randn_bf16((self.batch, HEADS, CHAIN_S, HEAD_DIM), gen, device)
-        self.k = randn_bf16((self.batch, HEADS, CHAIN_S, HEAD_DIM), gen, device)
+        qk = (self.batch, CHAIN_S, HEADS, HEAD_DIM) if token_major else (self.batch, HEADS, CHAIN_S, HEAD_DIM)
+        self.q = randn_bf16(qk, gen, device)
+        self.k = randn_bf16(qk, gen, device)
         self.o = randn_bf16((T, HIDDEN), gen, device)
         self.gate = randn_bf16((T, INTER), gen, device, 0.5)
         self.up = randn_bf16((T, INTER), gen, device, 0.5)
@@ -201,31 +208,35 @@ class Chain:
         self.footprint = per["op_sum"] * T
         self.config = {"workload": "chain: embed+RMSNorm -> RoPE -> add+RMSNorm -> SwiGLU",
                        "tokens_per_gpu": T, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM,
-                       "intermediate": INTER, "vocab": VOCAB, "qk_layout": [self.batch, HEADS, CHAIN_S, HEAD_DIM],
+                       "intermediate": INTER, "vocab": VOCAB, "qk_shape": list(qk),
+                       "qk_layout": "token-major [B, S, heads, head_dim]" if token_major
+                       else "head-major [B, heads, S, head_dim]",
                        "bytes_per_token_minimal": per["minimal"], "bytes_per_token_moved": per["op_sum"],
                        "l2": f"inputs larger than L2 ({per['op_sum'] * T / 1e9:.1f} GB moved per step vs 126 MB L2); no flush"}
 
     def step(self, stream=None, events=None):
         self.chain.run_device(self.w, self.ids, self.q, self.k, self.o, self.gate, self.up, self.h, self.n1,
-                              self.r, self.n2, self.y, 0, stream=stream, events=events)
+                              self.r, self.n2, self.y, 0, stream=stream, events=events,
+                              token_major=self.token_major)
         return len(self.kernels)
 
     # -- decode shape (64 tokens, offset 4095), launch-latency bound: CUDA graph
     def decode_latency_us(self, iters=200):
         torch = self.torch
         T = DECODE_B
-        dq = self.q[:1, :, :DECODE_B].reshape(DECODE_B, HEADS, 1, HEAD_DIM).clone()  # [64, 16, 1, 128]
+        shape = (DECODE_B, 1, HEADS, HEAD_DIM) if self.token_major else (DECODE_B, HEADS, 1, HEAD_DIM)
+        dq = self.q.reshape(-1)[:DECODE_B * HEADS * HEAD_DIM].reshape(shape).clone()
         dk = dq.clone()
         args = (self.ids[:T], dq, dk, self.o[:T], self.gate[:T], self.up[:T], self.h[:T], self.n1[:T],
                 self.r[:T], self.n2[:T], self.y[:T])
         s = torch.cuda.Stream(self.device)
         with torch.cuda.stream(s):
             for _ in range(3):
-                self.chain.run_device(self.w, *args, 4095, stream=s)
+                self.chain.run_device(self.w, *args, 4095, stream=s, token_major=self.token_major)
         s.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
-            self.chain.run_device(self.w, *args, 4095, stream=s)
+            self.chain.run_device(self.w, *args, 4095, stream=s, token_major=self.token_major)
         for _ in range(10):
             g.replay()
         torch.cuda.synchronize()
@@ -242,8 +253,8 @@ class Chain:
     # -- end to end: pinned host buffers through the public API
     def e2e(self, steps):
         torch = self.torch
-        hc = self.chain.HostChain(self.w, self.batch, HEADS, CHAIN_S, HEAD_DIM, HIDDEN, INTER, chunk_batches=1,
-                                  device=self.device)
+        hc = self.chain.HostChain(self.w, self.batch, HEADS, CHAIN_S, HEAD_DIM, HIDDEN, INTER,
+                                  chunk_tokens=self.chunk_tokens, token_major=self.token_major, device=self.device)
         pin = dict(pin_memory=True)
         host_in = {n: torch.empty(getattr(self, n).shape, dtype=getattr(self, n).dtype, **pin)
                    for n in hc.IN}
@@ -515,7 +526,10 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
-    wl = Chain(device, rank, args.tokens) if args.workload == "chain" else SingleOp(args.workload, device, rank)
+    if args.workload == "chain":
+        wl = Chain(device, rank, args.tokens, args.qk_layout == "token", args.chunk_tokens)
+    else:
+        wl = SingleOp(args.workload, device, rank)
     stream = torch.cuda.current_stream(device)
 
     for _ in range(args.warmup):

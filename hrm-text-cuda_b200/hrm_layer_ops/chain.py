@@ -4,15 +4,15 @@ One pass over T tokens runs the four kernels the HRM layer loop uses between
 its GEMMs (src/lib.rs:1191-1200, 969, 828, 976-979, 998):
 
     h, n1  = embed_rms_norm(ids, table, scale, w1)     embedding gather + RMSNorm
-    q, k   = rope_embed(q, k, offset, table)          in place, [B, 16, S, 128]
+    q, k   = rope_embed(q, k, offset, table)          in place, [B, 16, S, 128] or [B, S, 16, 128]
     r, n2  = add_rms_norm(h, o, w2)                   residual add + RMSNorm
     y      = swiglu_ffn(gate, up)
 
 `run_device` queues the four launches on one stream.  `HostChain` takes
-pinned host buffers and streams the pass through the GPU in chunks of whole
-Q/K batches: chunk i+1 is copied in while chunk i computes and chunk i-1 is
-copied out, on three streams ordered by events, so PCIe traffic in both
-directions overlaps the kernels.
+pinned host buffers and streams the pass through the GPU in chunks of tokens:
+chunk i+1 is copied in while chunk i computes and chunk i-1 is copied out, on
+three streams ordered by events, so PCIe traffic in both directions overlaps
+the kernels.
 """
 
 from __future__ import annotations
@@ -56,8 +56,14 @@ def algorithmic_bytes_per_token(hidden: int, heads: int, head_dim: int, inter: i
 
 
 def run_device(w: ChainWeights, ids, q, k, o, gate, up, h, n1, r, n2, y, offset: int = 0,
-               stream: Optional[torch.cuda.Stream] = None, events: Optional[List] = None) -> None:
-    """Queues the four launches; `events` (5 CUDA events) brackets each kernel if given."""
+               stream: Optional[torch.cuda.Stream] = None, events: Optional[List] = None,
+               token_major: bool = False) -> None:
+    """Queues the four launches; `events` (5 CUDA events) brackets each kernel if given.
+
+    q, k are [batch, heads, seq, head_dim] (the reference's layout) or, with
+    token_major, [batch, seq, heads, head_dim]; token s is at position
+    offset + s.
+    """
     def mark(i):
         if events is not None:
             events[i].record(stream)
@@ -65,7 +71,10 @@ def run_device(w: ChainWeights, ids, q, k, o, gate, up, h, n1, r, n2, y, offset:
     mark(0)
     ops.embed_rms_norm(ids, w.table, w.scale, w.w1, w.eps, hidden_out=h, normed_out=n1, stream=stream)
     mark(1)
-    ops.rope_embed(q, k, offset, w.theta, w.rope, stream=stream)
+    if token_major:
+        ops.rope_embed_token_major(q, k, offset, w.theta, w.rope, stream=stream)
+    else:
+        ops.rope_embed(q, k, offset, w.theta, w.rope, stream=stream)
     mark(2)
     ops.add_rms_norm(h, o, w.w2, w.eps, residual_out=r, normed_out=n2, stream=stream)
     mark(3)
@@ -74,30 +83,41 @@ def run_device(w: ChainWeights, ids, q, k, o, gate, up, h, n1, r, n2, y, offset:
 
 
 class HostChain:
-    """Runs the chain on pinned host tensors, chunked by Q/K batch.
+    """Runs the chain on pinned host tensors, streaming it through the GPU in chunks.
 
-    Host inputs:  ids [T] int32, q, k [B, heads, S, hd] bf16, o [T, hidden],
-                  gate, up [T, inter]      (T = B * S; rows of batch b are b*S..)
-    Host outputs: q, k (rotated, written back in place), h, n1, r, n2 [T, hidden],
-                  y [T, inter].
-    Device staging: two slots of every per-chunk buffer (double buffering).
+    Host inputs:  ids [T] int32, q, k bf16, o [T, hidden], gate, up [T, inter]
+    Host outputs: q, k (rotated), h, n1, r, n2 [T, hidden], y [T, inter]
+    (T = batch * seq; token t is position t % seq of sequence t // seq).
+
+    Token-major q, k ([batch, seq, heads, head_dim]) let every tensor be cut
+    into contiguous ranges of `chunk_tokens` tokens (a divisor of seq), each
+    rotated at its own position offset; head-major q, k ([batch, heads, seq,
+    head_dim]) are cut into whole sequences.  Two device slots of every
+    per-chunk buffer alternate (double buffering).  A slot is refilled only
+    after the copies out of it -- from this pass or the previous one -- have
+    finished, so consecutive passes may overlap: one pass's last copies out
+    run under the next pass's first copies in.
     """
 
+    IN = ("ids", "q", "k", "o", "gate", "up")
+    OUT = ("q", "k", "h", "n1", "r", "n2", "y")
+
     def __init__(self, weights: ChainWeights, batch: int, heads: int, seq: int, head_dim: int, hidden: int,
-                 inter: int, chunk_batches: int = 1, device=None):
+                 inter: int, chunk_tokens: Optional[int] = None, token_major: bool = True, device=None):
         self.w = weights
         self.B, self.heads, self.S, self.hd = batch, heads, seq, head_dim
         self.hidden, self.inter = hidden, inter
-        self.cb = chunk_batches
-        if batch % chunk_batches:
-            raise ValueError("batch must be a multiple of chunk_batches")
+        self.token_major = token_major
+        self.ct = (chunk_tokens or seq) if token_major else seq
+        if seq % self.ct:
+            raise ValueError("chunk_tokens must divide seq")
         self.device = torch.device(device if device is not None else "cuda")
-        ct = chunk_batches * seq
+        ct = self.ct
         bf = dict(dtype=torch.bfloat16, device=self.device)
+        qk_shape = (1, ct, heads, head_dim) if token_major else (1, heads, seq, head_dim)
         self.slots = [dict(
             ids=torch.empty(ct, dtype=torch.int32, device=self.device),
-            q=torch.empty((chunk_batches, heads, seq, head_dim), **bf),
-            k=torch.empty((chunk_batches, heads, seq, head_dim), **bf),
+            q=torch.empty(qk_shape, **bf), k=torch.empty(qk_shape, **bf),
             o=torch.empty((ct, hidden), **bf), gate=torch.empty((ct, inter), **bf),
             up=torch.empty((ct, inter), **bf), h=torch.empty((ct, hidden), **bf),
             n1=torch.empty((ct, hidden), **bf), r=torch.empty((ct, hidden), **bf),
@@ -105,44 +125,45 @@ class HostChain:
         self.s_in = torch.cuda.Stream(self.device)
         self.s_cmp = torch.cuda.Stream(self.device)
         self.s_out = torch.cuda.Stream(self.device)
-
-    IN = ("ids", "q", "k", "o", "gate", "up")
-    OUT = ("q", "k", "h", "n1", "r", "n2", "y")
+        self.slot_free = [None, None]  # per slot: event after the last copies out of it
 
     def bytes_per_pass(self, host_in: Dict[str, torch.Tensor], host_out: Dict[str, torch.Tensor]):
         return (sum(host_in[n].numel() * host_in[n].element_size() for n in self.IN),
                 sum(host_out[n].numel() * host_out[n].element_size() for n in self.OUT))
 
     def _chunk(self, t: torch.Tensor, name: str, c: int) -> torch.Tensor:
+        t0, t1 = c * self.ct, (c + 1) * self.ct
         if name in ("q", "k"):
-            return t[c * self.cb:(c + 1) * self.cb]
-        ct = self.cb * self.S
-        return t[c * ct:(c + 1) * ct]
+            if self.token_major:
+                return t.view(1, self.B * self.S, self.heads, self.hd)[:, t0:t1]
+            return t[c:c + 1]
+        return t[t0:t1]
 
     def run(self, host_in: Dict[str, torch.Tensor], host_out: Dict[str, torch.Tensor], offset: int = 0) -> int:
         """Queues the whole pass; returns the number of kernel launches queued."""
-        n_chunks = self.B // self.cb
-        loaded = [torch.cuda.Event() for _ in range(n_chunks)]
-        computed = [torch.cuda.Event() for _ in range(n_chunks)]
-        drained = [torch.cuda.Event() for _ in range(n_chunks)]
+        n_chunks = self.B * self.S // self.ct
         launches = 0
         for c in range(n_chunks):
             slot = self.slots[c % 2]
+            loaded, computed, drained = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
             with torch.cuda.stream(self.s_in):
-                if c >= 2:
-                    self.s_in.wait_event(drained[c - 2])  # slot free again
+                if self.slot_free[c % 2] is not None:
+                    self.s_in.wait_event(self.slot_free[c % 2])  # copies out of this slot are done
                 for n in self.IN:
                     slot[n].copy_(self._chunk(host_in[n], n, c), non_blocking=True)
-                loaded[c].record(self.s_in)
-            self.s_cmp.wait_event(loaded[c])
+                loaded.record(self.s_in)
+            self.s_cmp.wait_event(loaded)
+            pos = offset + (c * self.ct) % self.S if self.token_major else offset
             run_device(self.w, slot["ids"], slot["q"], slot["k"], slot["o"], slot["gate"], slot["up"], slot["h"],
-                       slot["n1"], slot["r"], slot["n2"], slot["y"], offset, stream=self.s_cmp)
+                       slot["n1"], slot["r"], slot["n2"], slot["y"], pos, stream=self.s_cmp,
+                       token_major=self.token_major)
             launches += len(CHAIN_KERNELS)
-            computed[c].record(self.s_cmp)
+            computed.record(self.s_cmp)
             with torch.cuda.stream(self.s_out):
-                self.s_out.wait_event(computed[c])
+                self.s_out.wait_event(computed)
                 for n in self.OUT:
                     self._chunk(host_out[n], n, c).copy_(slot[n], non_blocking=True)
-                drained[c].record(self.s_out)
+                drained.record(self.s_out)
+            self.slot_free[c % 2] = drained
         torch.cuda.current_stream(self.device).wait_stream(self.s_out)
         return launches
