@@ -46,6 +46,20 @@ __device__ __forceinline__ void st_stream(uint4* p, const uint4& v) { __stcs(p, 
 __device__ __forceinline__ uint4 ld_keep(const uint4* p) { return __ldg(p); }
 __device__ __forceinline__ float4 ld_keep(const float4* p) { return __ldg(p); }
 
+// ------------------------------------------- programmatic dependent launch
+// Every kernel calls this before its first global-memory access.  The wait
+// (griddepcontrol.wait) returns once the grid this launch depends on has
+// completed and its writes are visible; for a launch that was not
+// programmatic it returns at once.  The trigger (griddepcontrol.launch_
+// dependents) then lets the next programmatic launch in the stream be
+// scheduled while this grid still runs: its CTAs start once every CTA here has
+// passed this point and park in their own wait, so the launch latency of the
+// next kernel overlaps this one's execution instead of following it.
+__device__ __forceinline__ void grid_dependency_begin() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 // ---------------------------------------------------------- async staging
 // cp.async (LDGSTS) of one 16-byte chunk global -> shared, L2-cached only.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {

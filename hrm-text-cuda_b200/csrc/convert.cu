@@ -51,6 +51,7 @@ __device__ __forceinline__ uint16_t convert_one(uint32_t bits) {
 
 template <int DTYPE>
 __global__ void __launch_bounds__(kThreads) convert_vec_kernel(const uint4* src, uint4* dst, int64_t nvec) {
+  grid_dependency_begin();
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nvec; i += stride) {
     uint32_t in[8];
@@ -76,6 +77,7 @@ __global__ void __launch_bounds__(kThreads) convert_vec_kernel(const uint4* src,
 // Any alignment: element i's bytes assembled little-endian from src + i * size.
 template <int DTYPE>
 __global__ void __launch_bounds__(kThreads) convert_scalar_kernel(const uint8_t* src, uint16_t* dst, int64_t n) {
+  grid_dependency_begin();
   constexpr int kSize = DTYPE == HRM_DTYPE_F32 ? 4 : 2;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride) {
@@ -95,7 +97,7 @@ cudaError_t launch_dtype(const void* src, void* dst, int64_t n, cudaStream_t s) 
     if (nvec > 0) {
       int64_t blocks = (nvec + kThreads - 1) / kThreads;
       if (blocks > cap) blocks = cap;
-      convert_vec_kernel<DTYPE><<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<const uint4*>(src),
+      launch_kernel(convert_vec_kernel<DTYPE>, blocks, kThreads, 0, s, static_cast<const uint4*>(src),
                                                                       static_cast<uint4*>(dst), nvec);
       done = nvec * 8;
     }
@@ -105,7 +107,7 @@ cudaError_t launch_dtype(const void* src, void* dst, int64_t n, cudaStream_t s) 
     constexpr int kSize = DTYPE == HRM_DTYPE_F32 ? 4 : 2;
     int64_t blocks = (rest + kThreads - 1) / kThreads;
     if (blocks > cap) blocks = cap;
-    convert_scalar_kernel<DTYPE><<<(unsigned)blocks, kThreads, 0, s>>>(
+    launch_kernel(convert_scalar_kernel<DTYPE>, blocks, kThreads, 0, s,
         static_cast<const uint8_t*>(src) + done * kSize, static_cast<uint16_t*>(dst) + done, rest);
   }
   return cudaGetLastError();

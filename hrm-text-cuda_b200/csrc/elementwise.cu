@@ -59,6 +59,7 @@ struct GateOp {  // first operand: gate, second: attention output
 // read through L1 (every CTA reads the same few KB), stores streamed.
 __global__ void __launch_bounds__(kThreads) broadcast_vec_kernel(uint4* dst, const uint4* src, int64_t n_copies,
                                                                   int64_t chunks) {
+  grid_dependency_begin();
   const int64_t total = n_copies * chunks;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < total; i += stride)
@@ -67,6 +68,7 @@ __global__ void __launch_bounds__(kThreads) broadcast_vec_kernel(uint4* dst, con
 
 __global__ void __launch_bounds__(kThreads) broadcast_scalar_kernel(uint16_t* dst, const uint16_t* src,
                                                                     int64_t n_copies, int64_t vec_len) {
+  grid_dependency_begin();
   const int64_t total = n_copies * vec_len;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < total; i += stride) dst[i] = src[i % vec_len];
@@ -88,6 +90,7 @@ __device__ __forceinline__ uint4 apply8(const Op& op, const uint4& a, const uint
 template <class Op>
 __global__ void __launch_bounds__(kThreads, HRM_EW_MINBLOCKS) ew_vec_kernel(const uint4* a, const uint4* b, uint4* out,
                                                           int64_t nvec, int tail) {
+  grid_dependency_begin();
   const Op op;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -115,6 +118,7 @@ __global__ void __launch_bounds__(kThreads, HRM_EW_MINBLOCKS) ew_vec_kernel(cons
 template <class Op>
 __global__ void __launch_bounds__(kThreads) ew_scalar_kernel(const uint16_t* a, const uint16_t* b, uint16_t* out,
                                                              int64_t n) {
+  grid_dependency_begin();
   const Op op;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride)
@@ -130,13 +134,13 @@ cudaError_t launch_ew(const void* a, const void* b, void* out, int64_t n, cudaSt
     if (blocks < 1) blocks = 1;
     if (HRM_EW_WAVES > 0 && blocks > max_blocks * HRM_EW_WAVES) blocks = max_blocks * HRM_EW_WAVES;
     if (blocks > INT32_MAX) blocks = INT32_MAX;
-    ew_vec_kernel<Op><<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<const uint4*>(a),
+    launch_kernel(ew_vec_kernel<Op>, blocks, kThreads, 0, s, static_cast<const uint4*>(a),
                                                             static_cast<const uint4*>(b),
                                                             static_cast<uint4*>(out), nvec, (int)(n % 8));
   } else {
     int64_t blocks = (n + kThreads - 1) / kThreads;
     if (blocks > max_blocks) blocks = max_blocks;
-    ew_scalar_kernel<Op><<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<const uint16_t*>(a),
+    launch_kernel(ew_scalar_kernel<Op>, blocks, kThreads, 0, s, static_cast<const uint16_t*>(a),
                                                                static_cast<const uint16_t*>(b),
                                                                static_cast<uint16_t*>(out), n);
   }
@@ -163,12 +167,12 @@ cudaError_t launch_broadcast(void* dst, const void* src, int64_t n_copies, int64
     const int64_t chunks = vec_len / 8;
     int64_t blocks = (n_copies * chunks + kThreads - 1) / kThreads;
     if (blocks > cap) blocks = cap;
-    broadcast_vec_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<uint4*>(dst),
+    launch_kernel(broadcast_vec_kernel, blocks, kThreads, 0, s, static_cast<uint4*>(dst),
                                                                static_cast<const uint4*>(src), n_copies, chunks);
   } else {
     int64_t blocks = (n_copies * vec_len + kThreads - 1) / kThreads;
     if (blocks > cap) blocks = cap;
-    broadcast_scalar_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<uint16_t*>(dst),
+    launch_kernel(broadcast_scalar_kernel, blocks, kThreads, 0, s, static_cast<uint16_t*>(dst),
                                                                   static_cast<const uint16_t*>(src), n_copies,
                                                                   vec_len);
   }

@@ -31,6 +31,7 @@ constexpr int kInFlight = HRM_EMB_INFLIGHT;
 __global__ void __launch_bounds__(kThreads) embedding_warp_kernel(const uint32_t* ids, const uint4* table,
                                                                   uint4* out, int64_t tokens, int nchunks,
                                                                   uint32_t vocab, float scale) {
+  grid_dependency_begin();
   const int lane = threadIdx.x & 31;
   const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
   for (int64_t t = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); t < tokens; t += warp_stride) {
@@ -67,6 +68,7 @@ __global__ void __launch_bounds__(kThreads) embedding_scalar_kernel(const uint32
                                                                     uint16_t* out, int64_t tokens,
                                                                     int64_t hidden, uint32_t vocab,
                                                                     float scale) {
+  grid_dependency_begin();
   const int64_t n = tokens * hidden;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride) {
@@ -86,13 +88,13 @@ cudaError_t launch_embedding(const uint32_t* ids, const void* table, void* out, 
     int64_t blocks = (tokens + kWarps - 1) / kWarps;
     if (HRM_EMB_WAVES > 0 && blocks > wave * HRM_EMB_WAVES) blocks = wave * HRM_EMB_WAVES;
     if (blocks > INT32_MAX) blocks = INT32_MAX;
-    embedding_warp_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(ids, static_cast<const uint4*>(table),
+    launch_kernel(embedding_warp_kernel, blocks, kThreads, 0, s, ids, static_cast<const uint4*>(table),
                                                                  static_cast<uint4*>(out), tokens,
                                                                  (int)(hidden / 8), (uint32_t)vocab, scale);
   } else {
     int64_t blocks = (tokens * hidden + kThreads - 1) / kThreads;
     if (blocks > wave) blocks = wave;
-    embedding_scalar_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(ids, static_cast<const uint16_t*>(table),
+    launch_kernel(embedding_scalar_kernel, blocks, kThreads, 0, s, ids, static_cast<const uint16_t*>(table),
                                                                    static_cast<uint16_t*>(out), tokens, hidden,
                                                                    (uint32_t)vocab, scale);
   }

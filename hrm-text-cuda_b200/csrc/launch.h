@@ -13,6 +13,33 @@ int device_sm_count();
 // True when p is 16-byte aligned (a uint4 access is legal).
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Programmatic dependent launches (1) or plain stream-ordered ones (0).
+#ifndef HRM_PDL
+#define HRM_PDL 1
+#endif
+
+// Launches kernel k as grid x block threads with smem dynamic shared bytes on
+// stream s.  The launch is programmatic (cudaLaunchAttributeProgrammatic-
+// StreamSerialization): it may start before the previous kernel in s has
+// finished, which is safe because every kernel of this library waits for that
+// kernel at its entry (grid_dependency_begin).  Errors are left for
+// cudaGetLastError, as a triple-chevron launch leaves them.
+template <typename... KArgs, typename... Args>
+inline void launch_kernel(void (*k)(KArgs...), int64_t grid, int block, size_t smem, cudaStream_t s,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = HRM_PDL ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, k, static_cast<Args&&>(args)...);
+}
+
 cudaError_t launch_additive_inject(const void* a, const void* b, void* out, int64_t n, cudaStream_t s);
 cudaError_t launch_attn_gate(const void* gate, const void* attn, void* out, int64_t n, cudaStream_t s);
 cudaError_t launch_broadcast(void* dst, const void* src, int64_t n_copies, int64_t vec_len, cudaStream_t s);

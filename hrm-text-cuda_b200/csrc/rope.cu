@@ -127,6 +127,7 @@ __device__ __forceinline__ void load_cos_sin(const float4* table, int pos, int j
 
 template <bool TABLE>
 __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel(const RopeArgs a) {
+  grid_dependency_begin();
   const int j = threadIdx.x % a.g;
   const int rest = threadIdx.x / a.g;
   const int slice = rest % a.ht;
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel
 __global__ void __launch_bounds__(256) rope_scalar_kernel(uint16_t* q, uint16_t* k, int64_t rows, int64_t seq,
                                                           int64_t heads_inner, int head_dim, int offset,
                                                           float theta, const float* table) {
+  grid_dependency_begin();
   const int half = head_dim / 2;
   const int64_t total = rows * half;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -212,6 +214,7 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(uint16_t* q, uint16_t*
 
 __global__ void __launch_bounds__(256) rope_table_kernel(float* table, int64_t positions, int head_dim,
                                                          float theta) {
+  grid_dependency_begin();
   const int half = head_dim / 2;
   const int64_t total = positions * half;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -255,6 +258,7 @@ struct SplitArgs {
 
 template <bool TABLE, bool CACHE>
 __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) split_rope_tile_kernel(const SplitArgs a) {
+  grid_dependency_begin();
   const int j = threadIdx.x % a.g;
   const int rest = threadIdx.x / a.g;
   const int slice = rest % a.ht;
@@ -309,6 +313,7 @@ __global__ void __launch_bounds__(256) split_rope_scalar_kernel(
     const uint16_t* gqkv, uint16_t* gate, uint16_t* q, uint16_t* k, uint16_t* v, uint16_t* kc, uint16_t* vc,
     int64_t batch, int64_t seq, int heads, int head_dim, int offset, float theta, const float* table,
     int64_t cache_len, int64_t cache_offset) {
+  grid_dependency_begin();
   const int half = head_dim / 2;
   const int64_t total = batch * heads * seq * half;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -393,14 +398,14 @@ cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t 
     if (HRM_ROPE_CAP > 0 && blocks > sms * HRM_ROPE_CAP) blocks = sms * HRM_ROPE_CAP;
     if (blocks > INT32_MAX) blocks = INT32_MAX;
     if (table != nullptr)
-      rope_tile_kernel<true><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+      launch_kernel(rope_tile_kernel<true>, blocks, kThreads, 0, s, a);
     else
-      rope_tile_kernel<false><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+      launch_kernel(rope_tile_kernel<false>, blocks, kThreads, 0, s, a);
   } else {
     const int64_t rows = batch * heads * seq;
     int64_t blocks = (rows * (head_dim / 2) + 255) / 256;
     if (blocks > sms * 8) blocks = sms * 8;
-    rope_scalar_kernel<<<(unsigned)blocks, 256, 0, s>>>(static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), rows,
+    launch_kernel(rope_scalar_kernel, blocks, 256, 0, s, static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), rows,
                                                         seq, token_major ? heads : 1, (int)head_dim, (int)offset,
                                                         theta, table);
   }
@@ -411,7 +416,7 @@ cudaError_t launch_rope_table(float* table, int64_t positions, int64_t head_dim,
   int64_t blocks = (positions * (head_dim / 2) + 255) / 256;
   const int64_t cap = (int64_t)device_sm_count() * 8;
   if (blocks > cap) blocks = cap;
-  rope_table_kernel<<<(unsigned)blocks, 256, 0, s>>>(table, positions, (int)head_dim, theta);
+  launch_kernel(rope_table_kernel, blocks, 256, 0, s, table, positions, (int)head_dim, theta);
   return cudaGetLastError();
 }
 
@@ -453,19 +458,19 @@ cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, vo
     if (blocks > INT32_MAX) blocks = INT32_MAX;
     if (table != nullptr) {
       if (kc != nullptr)
-        split_rope_tile_kernel<true, true><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+        launch_kernel(split_rope_tile_kernel<true, true>, blocks, kThreads, 0, s, a);
       else
-        split_rope_tile_kernel<true, false><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+        launch_kernel(split_rope_tile_kernel<true, false>, blocks, kThreads, 0, s, a);
     } else {
       if (kc != nullptr)
-        split_rope_tile_kernel<false, true><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+        launch_kernel(split_rope_tile_kernel<false, true>, blocks, kThreads, 0, s, a);
       else
-        split_rope_tile_kernel<false, false><<<(unsigned)blocks, kThreads, 0, s>>>(a);
+        launch_kernel(split_rope_tile_kernel<false, false>, blocks, kThreads, 0, s, a);
     }
   } else {
     int64_t blocks = (batch * heads * seq * (head_dim / 2) + 255) / 256;
     if (blocks > sms * 8) blocks = sms * 8;
-    split_rope_scalar_kernel<<<(unsigned)blocks, 256, 0, s>>>(
+    launch_kernel(split_rope_scalar_kernel, blocks, 256, 0, s,
         static_cast<const uint16_t*>(gqkv), static_cast<uint16_t*>(gate), static_cast<uint16_t*>(q),
         static_cast<uint16_t*>(k), static_cast<uint16_t*>(v), static_cast<uint16_t*>(kc), static_cast<uint16_t*>(vc),
         batch, seq, (int)heads, (int)head_dim, (int)offset, theta, table, cache_len, cache_offset);

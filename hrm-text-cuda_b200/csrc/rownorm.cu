@@ -174,6 +174,7 @@ __device__ __forceinline__ void stage_weight(uint4* s_w, const uint4* w, int nch
 // ------------------------------------------------------------ bf16 fast path
 template <int VPL, int MODE, bool HAS_W>
 __global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rownorm_warp_kernel(const RowArgs a) {
+  grid_dependency_begin();
   extern __shared__ uint4 s_w[];
   const int lane = threadIdx.x & 31;
   if (HAS_W) stage_weight(s_w, a.w, a.nchunks);
@@ -248,6 +249,7 @@ struct RowArgsF32 {
 
 template <int VPL, bool HAS_W>
 __global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rms_f32_warp_kernel(const RowArgsF32 a) {
+  grid_dependency_begin();
   extern __shared__ uint4 s_w4[];
   float4* s_w = reinterpret_cast<float4*>(s_w4);
   const int lane = threadIdx.x & 31;
@@ -324,6 +326,7 @@ template <> __device__ __forceinline__ void store_t<float>(void* p, int64_t i, f
 
 template <typename T, int MODE, bool HAS_W>
 __global__ void __launch_bounds__(kBlockThreads) rownorm_block_kernel(const RowArgsScalar a) {
+  grid_dependency_begin();
   __shared__ float s_sums[kBlockWarps];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
@@ -404,7 +407,7 @@ cudaError_t launch_warp_on(const RowArgs& a, cudaStream_t s) {
   const int64_t wave = (int64_t)device_sm_count() * o;
   if (HRM_RN_WAVES > 0 && blocks > wave * HRM_RN_WAVES) blocks = wave * HRM_RN_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;
-  kernel<<<(unsigned)blocks, kThreads, smem, s>>>(a);
+  launch_kernel(kernel, blocks, kThreads, smem, s, a);
   return cudaGetLastError();
 }
 
@@ -424,7 +427,7 @@ cudaError_t launch_block(const RowArgsScalar& a, cudaStream_t s) {
   int64_t blocks = a.rows;
   const int64_t cap = (int64_t)device_sm_count() * 64;
   if (blocks > cap) blocks = cap;
-  rownorm_block_kernel<T, MODE, HAS_W><<<(unsigned)blocks, kBlockThreads, 0, s>>>(a);
+  launch_kernel(rownorm_block_kernel<T, MODE, HAS_W>, blocks, kBlockThreads, 0, s, a);
   return cudaGetLastError();
 }
 
@@ -479,7 +482,7 @@ cudaError_t launch_f32_warp(const RowArgsF32& a, cudaStream_t s) {
   const int64_t wave = (int64_t)device_sm_count() * o;
   if (HRM_RN_WAVES > 0 && blocks > wave * HRM_RN_WAVES) blocks = wave * HRM_RN_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;
-  kernel<<<(unsigned)blocks, kThreads, smem, s>>>(a);
+  launch_kernel(kernel, blocks, kThreads, smem, s, a);
   return cudaGetLastError();
 }
 
