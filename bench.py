@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload chain|add_rms_norm|rms_norm_f32|rope|swiglu|embedding|split_rope|
-                                attn_gate|convert_f32]
+                                attn_gate|convert_f32|module]
 
 Default workload ("chain"): the chained layer-op pass on 65536 tokens per GPU
 -- embedding [32000 x 2048] ~ N(0, 0.02) gathered for ids ~ U[0, 32000) and
@@ -65,7 +65,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="chain",
                     choices=["chain", "add_rms_norm", "rms_norm_f32", "rope", "swiglu", "embedding", "split_rope",
-                             "attn_gate", "convert_f32"])
+                             "attn_gate", "convert_f32", "module"])
     ap.add_argument("--tokens", type=int, default=CHAIN_B * CHAIN_S,
                     help="chain tokens per GPU (a multiple of 4096; default 65536)")
     ap.add_argument("--qk-layout", choices=["token", "head"], default="token",
@@ -468,6 +468,82 @@ class SingleOp:
         return None
 
 
+class Module:
+    """One pass of a 4-layer H/L module over 16384 tokens: the layer loop's
+    residual / norm / SwiGLU schedule (hrm_layer_ops.module.transformer_module:
+    injection + pre-norm, then per layer add+norm, SwiGLU, add+norm).  The
+    attention and GEMM outputs are synthetic and pre-filled (their callbacks do
+    nothing), so the step times exactly the library's 13 launches."""
+
+    name = "module"
+    LAYERS, TOKENS = 4, 16384
+
+    def __init__(self, device, rank):
+        import torch
+
+        from hrm_layer_ops import module
+
+        self.torch, self.module, self.device = torch, module, device
+        gen = torch.Generator(device=device).manual_seed(3000 + rank)
+        T, L = self.TOKENS, self.LAYERS
+        self.sc = module.ModuleScratch(T, HIDDEN, INTER, device)
+        for t in (self.sc.a, self.sc.d):
+            t.copy_(randn_bf16(t.shape, gen, device))
+        for t in (self.sc.g, self.sc.u):
+            t.copy_(randn_bf16(t.shape, gen, device, 0.5))
+        self.za, self.zb = randn_bf16((T, HIDDEN), gen, device), randn_bf16((T, HIDDEN), gen, device)
+        self.out = torch.empty((T, HIDDEN), dtype=torch.bfloat16, device=device)
+        per = module.module_bytes_per_token(HIDDEN, INTER, L)
+        self.bytes_per_step, self.rows_per_step = per * T, T
+        self.kernels = ["module_pass"]
+        self.dominant = "module_pass"
+        self.kernel_bytes = {"module_pass": self.bytes_per_step}
+        self.footprint = self.bytes_per_step
+        self.launches = 1 + 3 * L
+        self.config = {"workload": f"layer-loop module pass, {L} layers x {T} tokens (H {HIDDEN}, I {INTER}): "
+                                   "injection+norm, per layer add+norm / SwiGLU / add+norm",
+                       "tokens": T, "layers": L, "bytes_per_token": per,
+                       "bytes_per_token_reference_order": module.reference_order_bytes_per_token(HIDDEN, INTER, L),
+                       "gemm_and_attention": "outputs pre-filled, not timed",
+                       "roofline_scope": "the whole pass (13 launches)",
+                       "l2": f"{per * T / 1e9:.1f} GB moved per step vs 126 MB L2; no flush"}
+
+    @staticmethod
+    def _noop(*_):
+        return None
+
+    def step(self, stream=None, events=None):
+        if events is not None:
+            events[0].record(stream)
+        self.module.transformer_module(self.za, self.zb, self.out, self.LAYERS, self._noop, self._noop,
+                                       self._noop, self.sc, eps=EPS, stream=stream)
+        if events is not None:
+            events[1].record(stream)
+        return self.launches
+
+    def e2e(self, steps):
+        """Per step: z_a and z_b from pinned host memory, the pass, the output back."""
+        torch = self.torch
+        host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (self.za, self.zb, self.out)]
+        host[0].copy_(self.za)
+        host[1].copy_(self.zb)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches = 0
+        for it in range(steps + 1):  # iteration 0 is the warm-up
+            if it == 1:
+                torch.cuda.synchronize()
+                t0.record()
+            self.za.copy_(host[0], non_blocking=True)
+            self.zb.copy_(host[1], non_blocking=True)
+            n = self.step()
+            launches += n if it else 0
+            host[2].copy_(self.out, non_blocking=True)
+        t1.record()
+        torch.cuda.synchronize()
+        nb = self.za.numel() * 2
+        return t0.elapsed_time(t1) / steps, 2 * nb, nb, launches
+
+
 # ------------------------------------------------------------------ main
 def reference_arm(args, rank):
     """The reference's path on the host cores: the oracle, all threads."""
@@ -528,6 +604,8 @@ def main():
 
     if args.workload == "chain":
         wl = Chain(device, rank, args.tokens, args.qk_layout == "token", args.chunk_tokens)
+    elif args.workload == "module":
+        wl = Module(device, rank)
     else:
         wl = SingleOp(args.workload, device, rank)
     stream = torch.cuda.current_stream(device)
@@ -576,7 +654,9 @@ def main():
             ms_e2e = float(t[0])
         e2e = {"value": round(world * wl.bytes_per_step / (ms_e2e / 1e3) / 1e9, 3), "unit": "GB/s",
                "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "pinned host buffers, H2D / kernels / D2H overlapped in chunks (public API)"}
+               "path": ("pinned host buffers, H2D / kernels / D2H overlapped in chunks (public API)"
+                        if isinstance(wl, Chain) else "pinned host buffers, H2D -> kernels -> D2H on one stream "
+                                                      "(public API)")}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and isinstance(wl, Chain):
         c = Chain.cpu_sample()

@@ -223,4 +223,40 @@ void HrmLayerOps::build_rope_table(size_t max_positions) {
   rope_positions_ = max_positions;
 }
 
+HrmLayerOps::ModuleScratch::ModuleScratch(const HrmLayerOps& ops, size_t rows_)
+    : rows(rows_),
+      x(ops.alloc_zero_bf16(rows_ * ops.config.hidden_size)),
+      n(ops.alloc_zero_bf16(rows_ * ops.config.hidden_size)),
+      n2(ops.alloc_zero_bf16(rows_ * ops.config.hidden_size)),
+      a(ops.alloc_zero_bf16(rows_ * ops.config.hidden_size)),
+      d(ops.alloc_zero_bf16(rows_ * ops.config.hidden_size)),
+      g(ops.alloc_zero_bf16(rows_ * ops.config.intermediate_size)),
+      u(ops.alloc_zero_bf16(rows_ * ops.config.intermediate_size)),
+      act(ops.alloc_zero_bf16(rows_ * ops.config.intermediate_size)) {}
+
+void HrmLayerOps::transformer_module(const CudaSlice<bf16>& z_a, const CudaSlice<bf16>& z_b, CudaSlice<bf16>& output,
+                                     size_t n_layers, const LayerCallbacks& layer, ModuleScratch& s) const {
+  const size_t rows = s.rows, hidden = config.hidden_size;
+  if (n_layers == 0) fail(HrmError::Kind::InvalidInput, HRM_ERR_INVALID_SHAPE, "transformer_module: no layers");
+  if (!layer.attention || !layer.gate_up || !layer.down)
+    fail(HrmError::Kind::InvalidInput, HRM_ERR_NULL_POINTER, "transformer_module: a layer callback is empty");
+  if (s.x.len() < rows * hidden || s.g.len() < rows * config.intermediate_size)
+    fail(HrmError::Kind::InvalidInput, HRM_ERR_INVALID_SHAPE,
+         "transformer_module: scratch was built for another hidden / intermediate size");
+  need(z_a, rows * hidden, "transformer_module", "z_a");
+  need(z_b, rows * hidden, "transformer_module", "z_b");
+  need(output, rows * hidden, "transformer_module", "output");
+  if (output.device_ptr() == z_b.device_ptr())
+    fail(HrmError::Kind::InvalidInput, HRM_ERR_ALIASING, "transformer_module: output aliases z_b");
+  add_rms_norm(z_a, z_b, s.x, s.n, nullptr, rows, hidden);
+  for (size_t i = 0; i < n_layers; ++i) {
+    layer.attention(i, s.n, s.a);
+    add_rms_norm(s.x, s.a, s.x, s.n2, nullptr, rows, hidden);
+    layer.gate_up(i, s.n2, s.g, s.u);
+    swiglu_ffn(s.g, s.u, s.act, rows * config.intermediate_size);
+    layer.down(i, s.act, s.d);
+    add_rms_norm(s.x, s.d, s.x, i + 1 == n_layers ? output : s.n, nullptr, rows, hidden);
+  }
+}
+
 }  // namespace hrm

@@ -14,6 +14,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -128,6 +129,35 @@ class HrmLayerOps {
                        CudaSlice<bf16>& v, CudaSlice<bf16>* k_cache, CudaSlice<bf16>* v_cache, size_t batch_size,
                        size_t seq_len, size_t num_heads, size_t head_dim, size_t position_offset, size_t cache_len,
                        size_t cache_offset) const;
+  // ---- the layer loop's residual / norm schedule
+  // Scratch of one module pass over `rows` tokens (the reference's
+  // ScratchBuffers, src/lib.rs:86-112): the residual stream x, the normed
+  // activations n / n2, the attention output a and the down projection d
+  // ([rows x hidden]); the FFN gate, up and activation ([rows x intermediate]).
+  struct ModuleScratch {
+    ModuleScratch(const HrmLayerOps& ops, size_t rows);
+    size_t rows;
+    CudaSlice<bf16> x, n, n2, a, d, g, u, act;
+  };
+  // The caller's attention and FFN GEMMs, queued on cu_stream().
+  struct LayerCallbacks {
+    std::function<void(size_t layer, const CudaSlice<bf16>& normed, CudaSlice<bf16>& attn_out)> attention;
+    std::function<void(size_t layer, const CudaSlice<bf16>& normed, CudaSlice<bf16>& gate, CudaSlice<bf16>& up)>
+        gate_up;
+    std::function<void(size_t layer, const CudaSlice<bf16>& act, CudaSlice<bf16>& down)> down;
+  };
+  // output = module(z_a + z_b): the cycle injection (src/lib.rs:1220-1229 or
+  // 1248-1256) and transformer_module (src/lib.rs:1036-1105, layers as
+  // src/lib.rs:955-1030) with every additive_inject -> rms_norm pair fused
+  // and no device copies:
+  //   (x, n) = add_rms_norm(z_a, z_b); per layer: attention(n) -> a,
+  //   (x, n2) = add_rms_norm(x, a), gate_up(n2), swiglu_ffn, down -> d,
+  //   (x, n) = add_rms_norm(x, d) -- into `output` after the last layer.
+  // Bit-identical to the reference's order.  `output` may be z_a (z_L = L(z_L +
+  // z_H) in place); it must not be z_b.
+  void transformer_module(const CudaSlice<bf16>& z_a, const CudaSlice<bf16>& z_b, CudaSlice<bf16>& output,
+                          size_t n_layers, const LayerCallbacks& layer, ModuleScratch& scratch) const;
+
   // Builds the fp32 cos/sin table for config.head_dim / config.rope_theta
   // covering positions [0, max_positions); rope_embed uses it from then on
   // for every call it covers, and evaluates angles in-kernel otherwise.

@@ -13,6 +13,7 @@
 #include "hrm_layer_ops.hpp"
 
 using hrm::bf16;
+using hrm::CudaSlice;
 using hrm::HrmError;
 using hrm::HrmLayerOps;
 
@@ -178,6 +179,108 @@ void test_invalid_input(HrmLayerOps& hrm) {
   expect(thrown, "odd head_dim rejected");
 }
 
+// transformer_module (the fused schedule) == the reference's order of wrapper
+// calls and device copies (src/lib.rs:955-1030 per layer, 1036-1105 per module,
+// 1215-1256 per cycle), bit for bit, over 2 H-cycles x 2 L-cycles of 3-layer
+// modules.  Stand-ins for attention and the FFN GEMMs are exact device copies:
+// a = n; gate = up = [n | n]; down = act[:, :hidden].
+void test_transformer_module(HrmLayerOps&) {
+  hrm::HrmConfig cfg;
+  cfg.hidden_size = 256;
+  cfg.intermediate_size = 512;
+  cfg.norm_eps = 1e-5f;
+  HrmLayerOps m(0, cfg);
+  const size_t rows = 64, H = 256, I = 512, L = 3, n = rows * H;
+  cudaStream_t st = m.cu_stream();
+  auto copy2d = [&](bf16* dst, size_t dpitch, const bf16* src, size_t spitch, size_t width) {
+    expect(cudaMemcpy2DAsync(dst, dpitch * sizeof(bf16), src, spitch * sizeof(bf16), width * sizeof(bf16), rows,
+                             cudaMemcpyDeviceToDevice, st) == cudaSuccess,
+           "cudaMemcpy2DAsync");
+  };
+  auto copy = [&](CudaSlice<bf16>& dst, const CudaSlice<bf16>& src) {
+    expect(cudaMemcpyAsync(dst.device_ptr(), src.device_ptr(), n * sizeof(bf16), cudaMemcpyDeviceToDevice, st) ==
+               cudaSuccess,
+           "cudaMemcpyAsync");
+  };
+  HrmLayerOps::LayerCallbacks cb;
+  cb.attention = [&](size_t, const CudaSlice<bf16>& nn, CudaSlice<bf16>& a) {
+    copy2d(a.device_ptr(), H, nn.device_ptr(), H, H);
+  };
+  cb.gate_up = [&](size_t, const CudaSlice<bf16>& nn, CudaSlice<bf16>& g, CudaSlice<bf16>& u) {
+    for (CudaSlice<bf16>* t : {&g, &u}) {
+      copy2d(t->device_ptr(), I, nn.device_ptr(), H, H);
+      copy2d(t->device_ptr() + H, I, nn.device_ptr(), H, H);
+    }
+  };
+  cb.down = [&](size_t, const CudaSlice<bf16>& act, CudaSlice<bf16>& d) {
+    copy2d(d.device_ptr(), H, act.device_ptr(), I, H);
+  };
+
+  // The reference's buffers and order.
+  auto tmp1 = m.alloc_zero_bf16(n), tmp2 = m.alloc_zero_bf16(n), norm_buf = m.alloc_zero_bf16(n);
+  auto attn_out = m.alloc_zero_bf16(n), norm2 = m.alloc_zero_bf16(n), down = m.alloc_zero_bf16(n);
+  auto res = m.alloc_zero_bf16(n), g = m.alloc_zero_bf16(rows * I), u = m.alloc_zero_bf16(rows * I);
+  auto act = m.alloc_zero_bf16(rows * I);
+  auto reference_module = [&](CudaSlice<bf16>& out, const CudaSlice<bf16>& z_b) {  // out = module(out + z_b)
+    m.additive_inject(out, z_b, tmp1, n);
+    copy(tmp2, tmp1);
+    for (size_t i = 0; i < L; ++i) {
+      CudaSlice<bf16>* x = &tmp2;
+      if (i > 0) {
+        copy(tmp1, out);
+        x = &tmp1;
+      }
+      m.rms_norm(*x, norm_buf, rows, H);
+      cb.attention(i, norm_buf, attn_out);
+      m.additive_inject(*x, attn_out, out, n);
+      m.rms_norm(out, norm2, rows, H);
+      cb.gate_up(i, norm2, g, u);
+      m.swiglu_ffn(g, u, act, rows * I);
+      cb.down(i, act, down);
+      m.additive_inject(out, down, res, n);
+      copy(out, res);
+    }
+    m.rms_norm(out, tmp1, rows, H);
+    copy(out, tmp1);
+  };
+
+  std::vector<bf16> h0(n), l0(n);
+  uint32_t state = 12345u;
+  for (size_t i = 0; i < n; ++i) {
+    state = state * 1664525u + 1013904223u;
+    h0[i] = bf16::from_f32(((state >> 8) * (1.0f / 16777216.0f)) * 4.0f - 2.0f);
+    state = state * 1664525u + 1013904223u;
+    l0[i] = bf16::from_f32(((state >> 8) * (1.0f / 16777216.0f)) * 4.0f - 2.0f);
+  }
+  auto rh = m.htod_copy_bf16(h0), rl = m.htod_copy_bf16(l0);
+  auto fh = m.htod_copy_bf16(h0), fl = m.htod_copy_bf16(l0);
+  HrmLayerOps::ModuleScratch scratch(m, rows);
+  for (int hc = 0; hc < 2; ++hc) {
+    for (int lc = 0; lc < 2; ++lc) {
+      reference_module(rl, rh);
+      m.transformer_module(fl, fh, fl, L, cb, scratch);
+    }
+    reference_module(rh, rl);
+    m.transformer_module(fh, fl, fh, L, cb, scratch);
+  }
+  const auto want_h = m.sync_reclaim(std::move(rh)), want_l = m.sync_reclaim(std::move(rl));
+  const auto got_h = m.sync_reclaim(std::move(fh)), got_l = m.sync_reclaim(std::move(fl));
+  size_t bad = 0;
+  for (size_t i = 0; i < n; ++i) bad += (got_h[i].bits != want_h[i].bits) + (got_l[i].bits != want_l[i].bits);
+  expect(bad == 0, std::to_string(bad) + " elements of z_H / z_L differ from the reference order");
+  bool finite = true;
+  for (size_t i = 0; i < n; ++i) finite = finite && std::isfinite(got_h[i].to_f32());
+  expect(finite, "z_H finite");
+
+  bool thrown = false;
+  try {
+    m.transformer_module(scratch.n, scratch.x, scratch.x, L, cb, scratch);
+  } catch (const HrmError& e) {
+    thrown = e.kind() == HrmError::Kind::InvalidInput && e.status() == HRM_ERR_ALIASING;
+  }
+  expect(thrown, "output aliasing z_b rejected");
+}
+
 }  // namespace
 
 int main() {
@@ -187,6 +290,7 @@ int main() {
       {"test_rope_embed", test_rope_embed},           {"test_add_rms_norm", test_add_rms_norm},
       {"test_split_gqkv_rope", test_split_gqkv_rope},
       {"test_invalid_input", test_invalid_input},
+      {"test_transformer_module", test_transformer_module},
   };
   try {
     HrmLayerOps hrm(0);

@@ -1,6 +1,8 @@
 """GPU: the C++ host layer's known-answer tests (tests/cpp/test_layer_ops.cpp),
 which restate the reference's own GPU tests (src/lib.rs:2225-2279) through
-the HrmLayerOps methods that mirror the reference's wrappers."""
+the HrmLayerOps methods that mirror the reference's wrappers, and check the
+C++ layer-loop schedule (transformer_module) against the reference's order of
+wrapper calls and device copies."""
 
 import os
 import subprocess
@@ -18,4 +20,4 @@ def test_cpp_host_known_answers():
     res = subprocess.run([exe], capture_output=True, text=True, timeout=120)
     print(res.stdout)
     assert res.returncode == 0, res.stdout + res.stderr
-    assert "all 8 tests passed" in res.stdout
+    assert "all 9 tests passed" in res.stdout

@@ -98,6 +98,34 @@ def test_rope_matches_reference(ref, oracle, rng, cuda, b, h, s, d, off, use_tab
         assert ulp_error(got, want, rope_pair_magnitude(want)).max() <= ULP_TOL
 
 
+class RefOps:
+    """The reference kernels as the operator set of reference_order_module."""
+
+    def __init__(self, ref):
+        self.ref = ref
+
+    def additive_inject(self, a, b, out):
+        self.ref.additive_inject(a, b, out)
+
+    def rms_norm(self, x, y, eps):
+        self.ref.rms_norm(x, y, eps)
+
+    def swiglu(self, g, u, out):
+        self.ref.swiglu_ffn(g, u, out)
+
+
+def test_module_schedule_matches_reference_kernels_in_reference_order(ref, cuda):
+    """The recurrent loop (2 H-cycles x 2 L-cycles of 2-layer modules, 1024
+    rows, H 2048, I 5632, cuBLAS stand-ins for attention and the FFN GEMMs) run
+    with the reference's kernels in the reference's order, device copies
+    included, equals hrm_layer_ops.module.transformer_module bit for bit."""
+    from test_module_schedule_gpu import run_both
+
+    (rh, rl), (fh, fl) = run_both(RefOps(ref), 1024, 2048, 5632, 2, cuda, seed=51)
+    assert torch.equal(fl.view(torch.int16), rl.view(torch.int16))
+    assert torch.equal(fh.view(torch.int16), rh.view(torch.int16))
+
+
 # ------------------------------------------------ speed vs the reference
 def _time(fn, iters=20, warmup=3):
     for _ in range(warmup):
@@ -110,6 +138,23 @@ def _time(fn, iters=20, warmup=3):
     t1.record()
     torch.cuda.synchronize()
     return t0.elapsed_time(t1) / iters
+
+
+def _time_graph(calls, replays=50):
+    """ms per call of `calls`, captured once into a CUDA graph and replayed."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for c in calls:  # warm-up outside the capture
+            c()
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for c in calls:
+            c()
+    ms = _time(g.replay, iters=replays)
+    del g
+    return ms / len(calls)
 
 
 def test_throughput_vs_reference_kernels(ref, cuda):
@@ -132,13 +177,14 @@ def test_throughput_vs_reference_kernels(ref, cuda):
     nbytes = 16384 * 2048 * 2 * 4
     res["add_rms_norm"] = (nbytes / _time(lambda: ops.add_rms_norm(x, b, None, 1e-5, residual_out=r, normed_out=y)),
                            nbytes / _time(lambda: (ref.additive_inject(x, b, r), ref.rms_norm(r, y, 1e-5))))
-    # RMSNorm bf16 [4096 x 2048] (8 rotating copies: 268 MB > L2)
+    # RMSNorm bf16 [4096 x 2048] (8 rotating copies: 268 MB > L2).  A call takes
+    # about 10 us on the GPU, as long as a Python launch takes on the host, so
+    # both sides run from a CUDA graph of the 8 calls.
     xs = [rn((4096, 2048)) for _ in range(8)]
     ys = [torch.empty_like(xs[0]) for _ in range(8)]
-    it = iter(range(10 ** 9))
     nb = 4096 * 2048 * 2 * 2
-    res["rms_norm"] = (nb / _time(lambda: (lambda i: ops.rms_norm(xs[i % 8], None, 1e-5, out=ys[i % 8]))(next(it))),
-                       nb / _time(lambda: (lambda i: ref.rms_norm(xs[i % 8], ys[i % 8], 1e-5))(next(it))))
+    res["rms_norm"] = (nb / _time_graph([lambda i=i: ops.rms_norm(xs[i], None, 1e-5, out=ys[i]) for i in range(8)]),
+                       nb / _time_graph([lambda i=i: ref.rms_norm(xs[i], ys[i], 1e-5) for i in range(8)]))
     # RoPE Q/K [8, 16, 4096, 128]: table path and in-kernel angles vs the reference
     q, k = rn((8, 16, 4096, 128)), rn((8, 16, 4096, 128))
     table = ops.rope_table(4096, 128)
@@ -181,6 +227,44 @@ def test_throughput_vs_reference_kernels(ref, cuda):
     nb = 65536 * (4 + 2 * 2 * 2048)
     res["embedding"] = (nb / _time(lambda: ops.embedding_lookup(ids, tab, 45.254834, out=eo)),
                         nb / _time(lambda: ref.embedding_lookup(ids, tab, eo, 45.254834)))
+    del tab, eo
+    # one 4-layer module pass over 16384 tokens (H 2048, I 5632), attention and
+    # GEMM outputs pre-filled (the stand-ins do nothing): the fused schedule vs
+    # the reference's kernels in the reference's order with its device copies.
+    # Bytes: the fused schedule's algorithmic bytes for both (the ratio is the
+    # time ratio).
+    from hrm_layer_ops.module import ModuleScratch, module_bytes_per_token, transformer_module
+    from test_module_schedule_gpu import make_bufs, reference_order_module
+
+    class NoGemm:
+        @staticmethod
+        def attention(i, n, out):
+            pass
+
+        @staticmethod
+        def gate_up(i, n, g_, u_):
+            pass
+
+        @staticmethod
+        def down(i, act, out):
+            pass
+
+    rows, L = 16384, 4
+    sc = ModuleScratch(rows, 2048, 5632, cuda)
+    for t_ in (sc.a, sc.d):
+        t_.copy_(rn(t_.shape, 0.5))
+    for t_ in (sc.g, sc.u):
+        t_.copy_(rn(t_.shape, 0.5))
+    bufs = make_bufs(rows, 2048, 5632, cuda)
+    for t_ in (bufs[3], bufs[5], bufs[6], bufs[8]):   # attn_out, g, u, down
+        t_.copy_(rn(t_.shape, 0.5))
+    za, zb, zo = rn((rows, 2048)), rn((rows, 2048)), torch.empty((rows, 2048), dtype=bf, device=cuda)
+    nb = rows * module_bytes_per_token(2048, 5632, L)
+    res["module_4_layers"] = (
+        nb / _time(lambda: transformer_module(za, zb, zo, L, NoGemm.attention, NoGemm.gate_up, NoGemm.down, sc,
+                                              eps=1e-5), iters=10),
+        nb / _time(lambda: reference_order_module(RefOps(ref), za, zb, zo, L, NoGemm, bufs, 1e-5), iters=10))
+    del sc, bufs
     out = {k: {"ours_gbs": round(a / 1e6, 1), "reference_gbs": round(b_ / 1e6, 1), "speedup": round(a / b_, 2)}
            for k, (a, b_) in res.items()}
     print(json.dumps({"vs_reference_kernels": out}))
