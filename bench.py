@@ -599,8 +599,30 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    peers = None
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        from hrm_layer_ops.shard import PeerMonitor
+
+        peers = PeerMonitor.for_default_group("hrm/bench")
+    try:
+        run_ours(args, world, rank, device, peers)
+    except BaseException as e:
+        if peers is not None:  # tell the other ranks before they wait in a collective
+            peers.fail(f"{type(e).__name__}: {e}")
+        raise
+
+
+def run_ours(args, world, rank, device, peers):
+    """This library's arm: warm-up, K timed steps, extras, one JSON line on rank 0.
+    Before each collective every rank checks its peers' heartbeats (host only),
+    so a rank that failed is reported instead of waited for."""
+    import torch
+    import torch.distributed as dist
+
+    def collective_point(phase):
+        if peers is not None:
+            peers.sync(phase, timeout_s=120)
 
     if args.workload == "chain":
         wl = Chain(device, rank, args.tokens, args.qk_layout == "token", args.chunk_tokens)
@@ -619,6 +641,7 @@ def main():
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches = 0
+    collective_point(1)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -628,6 +651,7 @@ def main():
             launches += wl.step(stream, evs[i])
         end.record(stream)
         torch.cuda.synchronize()
+    collective_point(2)
     if world > 1:
         dist.barrier()
     ms_total = start.elapsed_time(end)
@@ -648,6 +672,7 @@ def main():
     if not args.no_e2e:
         e2e_steps = max(2, min(args.steps, 5))
         ms_e2e, h2d, d2h, _ = wl.e2e(e2e_steps)
+        collective_point(3)
         if world > 1:
             t = torch.tensor([ms_e2e], device=device, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -663,6 +688,7 @@ def main():
         cpu = {"value": round(c["gbs"], 3), "unit": "GB/s", "cores": c["cores"], "kind": "port",
                "sample": c["sample"]}
 
+    collective_point(4)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -122,12 +122,17 @@ def add_rms_norm(x: torch.Tensor, branch: torch.Tensor, weight: Optional[torch.T
 
 
 def rope_table(max_positions: int, head_dim: int, theta: float = 10000.0,
-               device: Optional[torch.device] = None, *, stream=None) -> torch.Tensor:
+               device: Optional[torch.device] = None, out: Optional[torch.Tensor] = None, *,
+               stream=None) -> torch.Tensor:
     """fp32 [max_positions, head_dim] table: cos in [:, :hd/2], sin in [:, hd/2:]."""
-    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    table = torch.empty((max_positions, head_dim), dtype=torch.float32, device=device)
-    call("hrm_rope_table_build", _ptr(table), max_positions, head_dim, theta, _stream(table, stream))
-    return table
+    if out is None:
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        out = torch.empty((max_positions, head_dim), dtype=torch.float32, device=device)
+    _need(out, "out", (torch.float32,))
+    if out.numel() != max_positions * head_dim:
+        raise ValueError("out has the wrong size")
+    call("hrm_rope_table_build", _ptr(out), max_positions, head_dim, theta, _stream(out, stream))
+    return out
 
 
 def rope_embed(q: torch.Tensor, k: torch.Tensor, position_offset: int = 0, theta: float = 10000.0,

@@ -14,12 +14,19 @@ The collectives here are for timing and verification only: the maximum of
 per-rank times, and gathering shards (or their checksums) to compare against
 an unsharded run.  They work on any backend (gloo on CPU tensors, NCCL on
 CUDA tensors).
+
+Failure detection is on the host (PeerMonitor): before a collective, every
+rank publishes its step in the process group's key-value store and waits,
+with a deadline, for its peers' heartbeats.  A rank that failed, or stopped,
+is reported as PeerFailure before the survivors enter a collective that would
+wait for it; no GPU work is involved.
 """
 
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass
-from typing import List, Tuple
+from typing import List, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -82,3 +89,72 @@ def checksum(t: torch.Tensor) -> int:
     b = t.contiguous().view(torch.int16 if t.element_size() == 2 else torch.int32).reshape(-1).to(torch.int64)
     idx = torch.arange(b.numel(), device=b.device, dtype=torch.int64)
     return int(((b & 0xFFFF if t.element_size() == 2 else b) * (idx % 65521 + 1)).sum().item())
+
+
+class PeerFailure(RuntimeError):
+    """One or more peer ranks failed or stopped publishing heartbeats."""
+
+    def __init__(self, ranks: Sequence[int], reason: str):
+        super().__init__(f"rank(s) {list(ranks)}: {reason}")
+        self.ranks, self.reason = list(ranks), reason
+
+
+class PeerMonitor:
+    """Heartbeats through a c10d key-value store (host only).
+
+    beat(step) publishes this rank's step; wait_peers(step, timeout_s) returns
+    once every peer has published a step >= `step`, and raises PeerFailure as
+    soon as a peer has declared a failure (fail(reason)), or when the deadline
+    passes with peers missing, or when the store itself is unreachable (the rank
+    that hosts it is gone).  Call wait_peers between steps, before the next
+    collective, with no kernels or collectives in flight.
+    """
+
+    def __init__(self, store, rank: int, world: int, prefix: str = "hrm/peer"):
+        self.store, self.rank, self.world, self.prefix = store, rank, world, prefix
+
+    @classmethod
+    def for_default_group(cls, prefix: str = "hrm/peer") -> "PeerMonitor":
+        from torch.distributed import distributed_c10d as c10d
+
+        return cls(c10d._get_default_store(), dist.get_rank(), dist.get_world_size(), prefix)
+
+    def _hb(self, r: int) -> str:
+        return f"{self.prefix}/hb/{r}"
+
+    def _fail(self, r: int) -> str:
+        return f"{self.prefix}/fail/{r}"
+
+    def beat(self, step: int) -> None:
+        self.store.set(self._hb(self.rank), str(int(step)))
+
+    def fail(self, reason: str) -> None:
+        """Declares this rank failed (best effort: the store may be gone too)."""
+        try:
+            self.store.set(self._fail(self.rank), reason)
+        except Exception:  # noqa: BLE001 - nothing more to report through
+            pass
+
+    def wait_peers(self, step: int, timeout_s: float = 10.0, poll_s: float = 0.005) -> None:
+        deadline = time.monotonic() + timeout_s
+        pending = set(range(self.world)) - {self.rank}
+        try:
+            while pending:
+                for r in sorted(pending):
+                    if self.store.check([self._fail(r)]):
+                        raise PeerFailure([r], self.store.get(self._fail(r)).decode(errors="replace"))
+                    if self.store.check([self._hb(r)]) and int(self.store.get(self._hb(r))) >= step:
+                        pending.discard(r)
+                if pending and time.monotonic() > deadline:
+                    raise PeerFailure(sorted(pending), f"no heartbeat for step {step} within {timeout_s:g} s")
+                if pending:
+                    time.sleep(poll_s)
+        except PeerFailure:
+            raise
+        except Exception as e:  # noqa: BLE001 - an unreachable store is a failed peer
+            raise PeerFailure(sorted(pending), f"store unreachable: {type(e).__name__}: {e}") from e
+
+    def sync(self, step: int, timeout_s: float = 10.0) -> None:
+        """beat(step) then wait_peers(step)."""
+        self.beat(step)
+        self.wait_peers(step, timeout_s)

@@ -63,5 +63,47 @@ def main():
     sys.exit(0 if ok else 1)
 
 
+def dead_rank_main():
+    """Failure detection over NCCL: both ranks run step 0 (a sharded
+    add_rms_norm and the max-over-ranks all_reduce); rank 1 then leaves between
+    steps, with nothing in flight, without a word; rank 0 runs step 1's kernels
+    and must get PeerFailure from its heartbeat wait before it enters step 1's
+    collective.  Launched as plain processes (not torch.distributed.run, whose
+    agent would stop rank 0 as soon as rank 1 exits).  Prints 'detected: ...'."""
+    import time
+
+    from hrm_layer_ops.shard import PeerFailure, PeerMonitor
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=30), device_id=dev)
+    mon = PeerMonitor.for_default_group()
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn((512, 2048), generator=g, device=dev).to(torch.bfloat16)
+    b = torch.randn((512, 2048), generator=g, device=dev).to(torch.bfloat16)
+    r0, r1 = row_range(512, world, rank)
+    ops.add_rms_norm(x[r0:r1], b[r0:r1], None, 1e-5)
+    torch.cuda.synchronize()
+    mon.sync(0, timeout_s=30)
+    max_over_ranks(1.0, dev)
+    torch.cuda.synchronize()
+    if rank == 1:
+        os._exit(3)
+    ops.add_rms_norm(x[r0:r1], b[r0:r1], None, 1e-5)
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    try:
+        mon.sync(1, timeout_s=5)
+        print("no failure detected", flush=True)
+        os._exit(1)
+    except PeerFailure as e:
+        print(f"detected: {e} after {time.monotonic() - t0:.2f} s", flush=True)
+        os._exit(0)
+
+
 if __name__ == "__main__":
-    main()
+    if "--dead-rank" in sys.argv:
+        dead_rank_main()
+    else:
+        main()

@@ -137,3 +137,80 @@ def test_gloo_dead_rank_is_detected_within_timeout():
     assert procs[1].exitcode == 3
     kind, waited = q.get(timeout=5)
     assert kind != "no error" and waited < 60, (kind, waited)
+
+
+def test_peer_monitor_declared_and_silent_failures():
+    """In one process over a HashStore: a declared failure is reported at once;
+    a missing heartbeat at the deadline."""
+    import time
+
+    from hrm_layer_ops.shard import PeerFailure, PeerMonitor
+
+    st = dist.HashStore()
+    m0, m1 = PeerMonitor(st, 0, 2), PeerMonitor(st, 1, 2)
+    m1.beat(0)
+    m0.sync(0, timeout_s=1)
+    m1.fail("ValueError: injected")
+    with pytest.raises(PeerFailure, match="injected") as e:
+        m0.sync(1, timeout_s=30)
+    assert e.value.ranks == [1]
+    lone = PeerMonitor(dist.HashStore(), 0, 3)
+    t0 = time.monotonic()
+    with pytest.raises(PeerFailure, match="no heartbeat") as e:
+        lone.sync(0, timeout_s=0.3)
+    assert e.value.ranks == [1, 2] and time.monotonic() - t0 < 5
+
+
+def _monitored_worker(rank, world, port, mode, result_q):
+    """Step 0 completes on both ranks; then rank `mode`'s victim fails before
+    step 1 (declared, silent, or the store-hosting rank 0 dies) and the
+    survivor must raise PeerFailure before entering step 1's collective."""
+    import datetime
+    import time
+
+    sys.path[:0] = [ROOT, PKG]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from hrm_layer_ops.shard import PeerFailure, PeerMonitor, max_over_ranks
+
+    mon = PeerMonitor.for_default_group()
+    mon.sync(0, timeout_s=30)
+    max_over_ranks(float(rank))  # step 0's collective
+    victim = 0 if mode == "host_dies" else 1
+    if rank == victim:
+        if mode == "declared":
+            try:
+                raise ValueError("injected failure in step 1")
+            except ValueError as e:
+                mon.fail(f"{type(e).__name__}: {e}")
+        os._exit(3)
+    t0 = time.monotonic()
+    try:
+        mon.sync(1, timeout_s=3)
+        max_over_ranks(float(rank))
+        result_q.put(("no failure", time.monotonic() - t0))
+    except PeerFailure as e:
+        result_q.put((e.reason, time.monotonic() - t0))
+    result_q.close()
+    result_q.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["declared", "silent", "host_dies"])
+def test_gloo_peer_failure_detected_before_the_collective(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_monitored_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    victim = 0 if mode == "host_dies" else 1
+    assert procs[victim].exitcode == 3 and procs[1 - victim].exitcode == 0, [p.exitcode for p in procs]
+    reason, waited = q.get(timeout=5)
+    assert reason != "no failure"
+    if mode == "declared":
+        assert "injected failure" in reason and waited < 2.5, (reason, waited)
+    else:
+        assert waited < 10, (reason, waited)
