@@ -293,4 +293,9 @@ int hrm_convert_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, hr
   return cuda_status(hrm::launch_convert_to_bf16(src, src_dtype, dst, n, as_cuda(stream)));
 }
 
+int hrm_wait_timeouts(unsigned int* count, int reset) {
+  if (!count) return HRM_ERR_NULL_POINTER;
+  return cuda_status(hrm::rownorm_wait_timeouts(count, reset != 0));
+}
+
 }  // extern "C"

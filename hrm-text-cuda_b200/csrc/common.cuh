@@ -69,4 +69,84 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
+// ------------------------------------------- bulk copies (TMA engine), mbarriers
+// One-dimensional bulk copies global -> shared (cp.async.bulk, no tensor map,
+// no multicast) completing on an mbarrier's transaction count.  Source and
+// destination 16-byte aligned, size a multiple of 16 bytes.
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+// Makes initialised mbarriers visible to the bulk-copy (async) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+// One arrival plus `bytes` of expected transactions for the current phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before its
+// later bulk copies into the same shared memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+
+// Deadline of every mbarrier wait (nanoseconds of %globaltimer).  A wait that
+// runs out counts itself in g_wait_timeouts and returns false; a bulk copy of
+// valid, host-checked addresses completes in microseconds, so a timeout means
+// a defect, reported instead of hung on.
+#ifndef HRM_WAIT_LIMIT_NS
+#define HRM_WAIT_LIMIT_NS 1000000000ull
+#endif
+// Per translation unit; the host reads it with cudaMemcpyFromSymbol.
+static __device__ unsigned int g_wait_timeouts;
+
+// Whole-warp bounded wait for phase `parity` of the mbarrier at `bar`: true
+// once every lane has observed the completed phase, false (in every lane)
+// when the deadline passes first.
+__device__ __forceinline__ bool warp_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  uint64_t limit_ns = HRM_WAIT_LIMIT_NS) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    if (__any_sync(0xffffffffu, globaltimer_ns() - t0 > limit_ns)) return false;
+  }
+}
+
 }  // namespace hrm

@@ -67,4 +67,7 @@ cudaError_t launch_rope_table(float* table, int64_t max_pos, int64_t head_dim, f
 
 cudaError_t launch_convert_to_bf16(const void* src, int dtype, void* dst, int64_t n, cudaStream_t s);
 
+// Bounded waits that ran out in the row kernels (device counter); reset sets it to 0.
+cudaError_t rownorm_wait_timeouts(unsigned int* count, bool reset);
+
 }  // namespace hrm

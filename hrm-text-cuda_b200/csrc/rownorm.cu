@@ -236,6 +236,152 @@ __global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rownorm_warp_kerne
   }
 }
 
+// ---------------------------------------------- bf16 bulk-async (TMA engine) path
+// Opt-in build (-DHRM_RN_BULK=1); the register path above is the default.
+// Same rows, same lane layout and arithmetic as rownorm_warp_kernel, but the
+// input rows reach shared memory through the bulk-copy engine instead of the
+// warp's own loads.  Each warp runs its own pipeline over its rows
+// (kBkRows contiguous rows, or with kBkRows = 0 rows gw, gw + G, ... of a
+// persistent one-CTA-per-SM grid): kBkStages shared-memory stages of one row
+// (x, or a gathered table row) or two rows (x and branch), each completed by
+// an mbarrier transaction count.  Lane 0 keeps kBkStages rows in flight: as
+// soon as the warp has copied stage s into registers it refills s with the
+// row kBkStages ahead.  Stores are the warp's usual coalesced 512-byte spans.
+//
+// Measured on B200, add + RMSNorm over 65536 x 2048 rows in the chain: 6.23
+// TB/s at its best shape (4 rows per warp, 8 warps, 2 stages) and 5.79 TB/s
+// persistent, against 6.59 TB/s for the register path.  Bytes in flight are
+// the limit: the register path holds 16-24 warps x 16 KB per SM (its 117
+// registers per thread fill most of the 256 KB register file), while bulk
+// staging is capped by 227 KB of shared memory and adds a shared -> register
+// hop.  For pure streaming the register file is the larger staging buffer.
+//
+// In-place use (residual_out == x) stays safe: a row's copy completes before
+// any output of that row is written, and every row belongs to one warp.
+#ifndef HRM_BK_WARPS
+#define HRM_BK_WARPS 8
+#endif
+#ifndef HRM_BK_STAGES
+#define HRM_BK_STAGES 2
+#endif
+// Rows per warp (0: persistent grid, one CTA per SM, rows strided by the
+// grid's warp count) and resident CTAs per SM the shared memory is sized for.
+#ifndef HRM_BK_ROWS
+#define HRM_BK_ROWS 4
+#endif
+#ifndef HRM_BK_CTAS
+#define HRM_BK_CTAS 1
+#endif
+constexpr int kBkMaxWarps = HRM_BK_WARPS;
+constexpr int kBkStages = HRM_BK_STAGES;
+constexpr int kBkRows = HRM_BK_ROWS;
+
+template <int MODE>
+__device__ __forceinline__ void bk_issue(const RowArgs& a, uint4* stage, uint32_t bar, int64_t row,
+                                         uint64_t policy) {
+  const uint32_t row_bytes = (uint32_t)a.nchunks * 16u;
+  mbar_arrive_expect_tx(bar, (MODE == kAdd ? 2u : 1u) * row_bytes);
+  if (MODE == kEmbed) {
+    uint32_t id = a.ids[row];
+    if (id >= a.vocab) id = a.vocab - 1;  // src/kernels/embedding_lookup.cu:35
+    bulk_g2s(smem_addr(stage), a.x + (int64_t)id * a.nchunks, row_bytes, bar);  // table rows may repeat
+  } else {
+    bulk_g2s_hint(smem_addr(stage), a.x + row * a.nchunks, row_bytes, bar, policy);
+    if (MODE == kAdd) bulk_g2s_hint(smem_addr(stage + a.nchunks), a.b + row * a.nchunks, row_bytes, bar, policy);
+  }
+}
+
+template <int VPL, int MODE, bool HAS_W>
+__global__ void __launch_bounds__(32 * kBkMaxWarps, 1) rownorm_bulk_kernel(const RowArgs a) {
+  grid_dependency_begin();
+  extern __shared__ uint4 smem[];
+  constexpr int kRowsPerStage = MODE == kAdd ? 2 : 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int w_chunks = HAS_W ? a.nchunks : 0;
+  const int stage_chunks = kRowsPerStage * a.nchunks;
+  uint4* s_w = smem;
+  uint4* s_rows = smem + w_chunks + (int64_t)warp * kBkStages * stage_chunks;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + w_chunks + (int64_t)nwarps * kBkStages * stage_chunks) + warp * kBkStages;
+
+  if (HAS_W) {
+    for (int c = threadIdx.x; c < a.nchunks; c += blockDim.x) cp_async16(&s_w[c], a.w + c);
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+  }
+  // Row k of this warp: gw + k * G (persistent) or gw * kBkRows + k.
+  const int64_t gw = (int64_t)blockIdx.x * nwarps + warp;
+  const int64_t G = kBkRows > 0 ? 1 : (int64_t)gridDim.x * nwarps;
+  const int64_t row0 = kBkRows > 0 ? gw * kBkRows : gw;
+  int64_t K = 0;
+  if (row0 < a.rows) {
+    K = kBkRows > 0 ? a.rows - row0 : (a.rows - row0 + G - 1) / G;
+    if (kBkRows > 0 && K > kBkRows) K = kBkRows;
+  }
+  if (K == 0) return;
+  const uint64_t policy = l2_evict_first_policy();
+  if (lane == 0) {
+    for (int s = 0; s < kBkStages; ++s) mbar_init(smem_addr(&bars[s]), 1);
+    mbar_init_fence();
+    for (int s = 0; s < kBkStages && s < K; ++s)
+      bk_issue<MODE>(a, s_rows + s * stage_chunks, smem_addr(&bars[s]), row0 + s * G, policy);
+  }
+  __syncwarp();
+
+  for (int64_t k = 0; k < K; ++k) {
+    const int s = (int)(k % kBkStages);
+    const uint32_t parity = (uint32_t)((k / kBkStages) & 1);
+    if (!warp_wait_bounded(smem_addr(&bars[s]), parity)) {
+      // Report, then wait (bounded) for this warp's other copies still in
+      // flight so that none lands in shared memory after the CTA is gone.
+      if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
+      for (int64_t kk = k + 1; kk < K && kk < k + kBkStages; ++kk)
+        warp_wait_bounded(smem_addr(&bars[kk % kBkStages]), (uint32_t)((kk / kBkStages) & 1));
+      warp_wait_bounded(smem_addr(&bars[s]), parity);
+      return;
+    }
+    const uint4* sx = s_rows + s * stage_chunks;
+    uint4 v[VPL];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) {
+        v[j] = sx[c];
+        if (MODE == kAdd) v[j] = add8(v[j], sx[a.nchunks + c]);
+        if (MODE == kEmbed) v[j] = scale8(v[j], a.scale);
+      }
+    }
+    __syncwarp();  // every lane has read stage s
+    if (lane == 0 && k + kBkStages < K) {
+      fence_proxy_async_smem();
+      bk_issue<MODE>(a, s_rows + s * stage_chunks, smem_addr(&bars[s]), row0 + (k + kBkStages) * G, policy);
+    }
+    const int64_t base = (row0 + k * G) * a.nchunks;
+    float p[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) p[e] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) {
+        if (MODE == kAdd || (MODE == kEmbed && a.r != nullptr)) st_stream(a.r + base + c, v[j]);
+        accum8(p, v[j]);
+      }
+    }
+    const float inv = inv_rms(ref_tree_bf16(p), a.hidden, a.eps);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < a.nchunks) {
+        uint4 wv = make_uint4(0, 0, 0, 0);
+        if (HAS_W) wv = s_w[c];
+        st_stream(a.y + base + c, norm8<HAS_W>(v[j], inv, wv));
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------ fp32 fast path
 struct RowArgsF32 {
   const float4* x;
@@ -422,6 +568,80 @@ cudaError_t dispatch_vpl(const RowArgs& a, cudaStream_t s) {
   return launch_warp_on<16, MODE, HAS_W>(a, s);
 }
 
+// Bulk-async path on (1) or off (0, the default: the register path measured
+// faster) for the shapes it takes.
+#ifndef HRM_RN_BULK
+#define HRM_RN_BULK 0
+#endif
+
+// Opt-in dynamic shared memory per CTA of the current device, cached per device.
+int smem_optin_bytes() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  int v = (dev >= 0 && dev < 64) ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (v > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0) {
+    cudaGetLastError();
+    v = 48 * 1024;
+  }
+  if (dev >= 0 && dev < 64) cache[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
+// Warps per CTA of the bulk path (as many stage rings as fit, at most
+// kBkMaxWarps) and the dynamic shared memory they need; 0 warps: no fit.
+int bulk_plan(int nchunks, int rows_per_stage, bool has_w, size_t* smem) {
+  size_t cap = (size_t)smem_optin_bytes();
+  if (HRM_BK_CTAS > 1) {  // per-SM capacity shared by HRM_BK_CTAS CTAs, 1 KB reserved each
+    const size_t per_cta = (233472 - 1024 * (size_t)HRM_BK_CTAS) / HRM_BK_CTAS;
+    if (per_cta < cap) cap = per_cta;
+  }
+  const size_t wbytes = has_w ? (size_t)nchunks * 16 : 0;
+  const size_t per_warp = (size_t)kBkStages * ((size_t)rows_per_stage * nchunks * 16 + 8);
+  if (cap <= wbytes) return 0;
+  size_t w = (cap - wbytes) / per_warp;
+  if (w > (size_t)kBkMaxWarps) w = kBkMaxWarps;
+  *smem = wbytes + w * per_warp;
+  return (int)w;
+}
+
+template <int VPL, int MODE, bool HAS_W>
+cudaError_t launch_bulk_on(const RowArgs& a, int nwarps, size_t smem, cudaStream_t s) {
+  auto kernel = rownorm_bulk_kernel<VPL, MODE, HAS_W>;
+  static std::atomic<bool> opted[64];  // per device: the opt-in is per function and device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  if (dev < 0 || dev >= 64 || !opted[dev].load(std::memory_order_relaxed)) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin_bytes());
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) opted[dev].store(true, std::memory_order_relaxed);
+  }
+  int64_t blocks;
+  if (kBkRows > 0) {
+    const int64_t rows_per_cta = (int64_t)nwarps * kBkRows;
+    blocks = (a.rows + rows_per_cta - 1) / rows_per_cta;
+  } else {
+    blocks = (a.rows + nwarps - 1) / nwarps;
+    const int64_t sms = device_sm_count();
+    if (blocks > sms) blocks = sms;  // one CTA per SM, warps loop over their rows
+  }
+  if (blocks > INT32_MAX) blocks = INT32_MAX;
+  launch_kernel(kernel, blocks, 32 * nwarps, smem, s, a);
+  return cudaGetLastError();
+}
+
+template <int MODE, bool HAS_W>
+cudaError_t dispatch_bulk(const RowArgs& a, int nwarps, size_t smem, cudaStream_t s) {
+  const int need = (a.nchunks + 31) / 32;
+  if (need <= 1) return launch_bulk_on<1, MODE, HAS_W>(a, nwarps, smem, s);
+  if (need <= 2) return launch_bulk_on<2, MODE, HAS_W>(a, nwarps, smem, s);
+  if (need <= 4) return launch_bulk_on<4, MODE, HAS_W>(a, nwarps, smem, s);
+  if (need <= 6) return launch_bulk_on<6, MODE, HAS_W>(a, nwarps, smem, s);
+  if (need <= 8) return launch_bulk_on<8, MODE, HAS_W>(a, nwarps, smem, s);
+  return launch_bulk_on<16, MODE, HAS_W>(a, nwarps, smem, s);
+}
+
 template <typename T, int MODE, bool HAS_W>
 cudaError_t launch_block(const RowArgsScalar& a, cudaStream_t s) {
   int64_t blocks = a.rows;
@@ -451,6 +671,12 @@ cudaError_t launch_bf16_rows(const void* x, const void* b, const uint32_t* ids, 
     a.vocab = (uint32_t)vocab;
     a.scale = scale;
     a.eps = eps;
+    if (HRM_RN_BULK) {
+      size_t smem = 0;
+      const int nwarps = bulk_plan(a.nchunks, MODE == kAdd ? 2 : 1, w != nullptr, &smem);
+      if (nwarps >= 1)
+        return w ? dispatch_bulk<MODE, true>(a, nwarps, smem, s) : dispatch_bulk<MODE, false>(a, nwarps, smem, s);
+    }
     return w ? dispatch_vpl<MODE, true>(a, s) : dispatch_vpl<MODE, false>(a, s);
   }
   RowArgsScalar a;
@@ -497,6 +723,15 @@ cudaError_t dispatch_f32(const RowArgsF32& a, cudaStream_t s) {
 }
 
 }  // namespace
+
+cudaError_t rownorm_wait_timeouts(unsigned int* count, bool reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int));
+  if (e == cudaSuccess && reset) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(unsigned int));
+  }
+  return e;
+}
 
 cudaError_t launch_rms_norm_bf16(const void* x, void* y, const void* w, int64_t rows, int64_t hidden, float eps,
                                  cudaStream_t s) {

@@ -20,6 +20,7 @@ from .ops import (  # noqa: F401
     rope_table,
     split_gqkv_rope,
     swiglu_ffn,
+    wait_timeouts,
 )
 
 __all__ = [
@@ -38,4 +39,5 @@ __all__ = [
     "gated_attn_output",
     "broadcast_vec",
     "convert_to_bf16",
+    "wait_timeouts",
 ]

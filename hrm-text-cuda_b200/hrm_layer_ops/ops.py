@@ -304,3 +304,11 @@ def convert_to_bf16(raw: torch.Tensor, dtype: str, out: Optional[torch.Tensor] =
         raise ValueError("out has the wrong size")
     call("hrm_convert_to_bf16", _ptr(raw), DTYPES[dtype], _ptr(out), n, _stream(raw, stream))
     return out
+
+
+def wait_timeouts(reset: bool = False) -> int:
+    """Bounded device waits that ran out (0 in correct operation); reads device
+    memory, so synchronize the streams that ran the library's kernels first."""
+    n = ctypes.c_uint(0)
+    call("hrm_wait_timeouts", ctypes.byref(n), int(reset))
+    return int(n.value)

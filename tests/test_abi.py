@@ -52,7 +52,7 @@ def test_python_front_end_binds_every_declared_symbol():
 
 
 def test_static_archive_and_cpp_host_built():
-    for f in ("lib/libhrm_ops.a", "lib/libhrm_host.a", "build/test_layer_ops"):
+    for f in ("lib/libhrm_ops.a", "lib/libhrm_host.a", "build/test_layer_ops", "build/test_wait_timeout"):
         assert os.path.exists(os.path.join(PKG, f)), f
 
 
@@ -90,6 +90,8 @@ def test_validation_negative_and_zero_sizes(lib):
 
 def test_validation_null_pointers(lib):
     from hrm_layer_ops import _lib
+
+    assert lib.hrm_wait_timeouts(None, 0) == _lib.HRM_ERR_NULL_POINTER
 
     assert lib.hrm_additive_inject(None, vp(B), vp(C), 8, None) == _lib.HRM_ERR_NULL_POINTER
     assert lib.hrm_rms_norm(vp(A), None, None, 1, 8, 1e-6, None) == _lib.HRM_ERR_NULL_POINTER

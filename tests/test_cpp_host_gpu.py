@@ -21,3 +21,15 @@ def test_cpp_host_known_answers():
     print(res.stdout)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "all 9 tests passed" in res.stdout
+
+
+def test_bounded_mbarrier_wait_self_test():
+    """tests/cpp/test_wait_timeout.cu: the deadline of the bulk-copy kernels'
+    mbarrier waits -- waits that complete return at once; a barrier nothing
+    completes returns false after 50 ms and is counted; the context stays usable."""
+    exe = os.path.join(PKG, "build", "test_wait_timeout")
+    assert os.path.exists(exe), "build with make -C hrm-text-cuda_b200"
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    print(res.stdout)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "all wait tests passed" in res.stdout

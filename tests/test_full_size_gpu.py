@@ -112,3 +112,5 @@ def test_chain_65536_tokens_and_decode(oracle, cuda):
         sel = torch.from_numpy(rows).to(cuda)
         g, u = to_host(dg[sel]), to_host(du[sel])
         assert ulp_error(to_host(out[sel]), oracle.swiglu_ffn(g, u)).max() <= ULP_TOL
+    torch.cuda.synchronize()
+    assert ops.wait_timeouts() == 0  # no bounded device wait ran out
