@@ -671,12 +671,12 @@ cudaError_t launch_bf16_rows(const void* x, const void* b, const uint32_t* ids, 
     a.vocab = (uint32_t)vocab;
     a.scale = scale;
     a.eps = eps;
-    if (HRM_RN_BULK) {
-      size_t smem = 0;
-      const int nwarps = bulk_plan(a.nchunks, MODE == kAdd ? 2 : 1, w != nullptr, &smem);
-      if (nwarps >= 1)
-        return w ? dispatch_bulk<MODE, true>(a, nwarps, smem, s) : dispatch_bulk<MODE, false>(a, nwarps, smem, s);
-    }
+#if HRM_RN_BULK
+    size_t smem = 0;
+    const int nwarps = bulk_plan(a.nchunks, MODE == kAdd ? 2 : 1, w != nullptr, &smem);
+    if (nwarps >= 1)
+      return w ? dispatch_bulk<MODE, true>(a, nwarps, smem, s) : dispatch_bulk<MODE, false>(a, nwarps, smem, s);
+#endif
     return w ? dispatch_vpl<MODE, true>(a, s) : dispatch_vpl<MODE, false>(a, s);
   }
   RowArgsScalar a;
