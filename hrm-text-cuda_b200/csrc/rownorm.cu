@@ -258,6 +258,12 @@ __global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rownorm_warp_kerne
 //
 // In-place use (residual_out == x) stays safe: a row's copy completes before
 // any output of that row is written, and every row belongs to one warp.
+// Bulk-async path on (1) or off (0, the default: the register path measured
+// faster) for the shapes it takes.
+#ifndef HRM_RN_BULK
+#define HRM_RN_BULK 0
+#endif
+#if HRM_RN_BULK
 #ifndef HRM_BK_WARPS
 #define HRM_BK_WARPS 8
 #endif
@@ -381,6 +387,8 @@ __global__ void __launch_bounds__(32 * kBkMaxWarps, 1) rownorm_bulk_kernel(const
     }
   }
 }
+
+#endif  // HRM_RN_BULK
 
 // ------------------------------------------------------------ fp32 fast path
 struct RowArgsF32 {
@@ -568,12 +576,7 @@ cudaError_t dispatch_vpl(const RowArgs& a, cudaStream_t s) {
   return launch_warp_on<16, MODE, HAS_W>(a, s);
 }
 
-// Bulk-async path on (1) or off (0, the default: the register path measured
-// faster) for the shapes it takes.
-#ifndef HRM_RN_BULK
-#define HRM_RN_BULK 0
-#endif
-
+#if HRM_RN_BULK
 // Opt-in dynamic shared memory per CTA of the current device, cached per device.
 int smem_optin_bytes() {
   static std::atomic<int> cache[64];
@@ -641,6 +644,8 @@ cudaError_t dispatch_bulk(const RowArgs& a, int nwarps, size_t smem, cudaStream_
   if (need <= 8) return launch_bulk_on<8, MODE, HAS_W>(a, nwarps, smem, s);
   return launch_bulk_on<16, MODE, HAS_W>(a, nwarps, smem, s);
 }
+
+#endif  // HRM_RN_BULK
 
 template <typename T, int MODE, bool HAS_W>
 cudaError_t launch_block(const RowArgsScalar& a, cudaStream_t s) {
