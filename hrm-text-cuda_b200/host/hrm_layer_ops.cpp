@@ -223,6 +223,57 @@ void HrmLayerOps::build_rope_table(size_t max_positions) {
   rope_positions_ = max_positions;
 }
 
+void HrmLayerOps::gated_attn_output(const CudaSlice<bf16>& gate, const CudaSlice<bf16>& attn_out,
+                                    CudaSlice<bf16>& output, size_t total_elements) const {
+  need(gate, total_elements, "gated_attn_output", "gate");
+  need(attn_out, total_elements, "gated_attn_output", "attn_out");
+  need(output, total_elements, "gated_attn_output", "output");
+  check(hrm_gated_attn_output(gate.device_ptr(), attn_out.device_ptr(), output.device_ptr(), (int64_t)total_elements,
+                              stream_),
+        "gated_attn_output");
+}
+
+void HrmLayerOps::apply_attn_gate(const CudaSlice<bf16>& gate, CudaSlice<bf16>& attn_out,
+                                  size_t total_elements) const {
+  need(gate, total_elements, "apply_attn_gate", "gate");
+  need(attn_out, total_elements, "apply_attn_gate", "attn_out");
+  check(hrm_apply_attn_gate(gate.device_ptr(), attn_out.device_ptr(), (int64_t)total_elements, stream_),
+        "apply_attn_gate");
+}
+
+void HrmLayerOps::broadcast_vec(CudaSlice<bf16>& dst, const CudaSlice<bf16>& src, size_t n_copies,
+                                size_t vec_len) const {
+  need(src, vec_len, "broadcast_vec", "src");
+  need(dst, n_copies * vec_len, "broadcast_vec", "dst");
+  check(hrm_broadcast_vec(dst.device_ptr(), src.device_ptr(), (int64_t)n_copies, (int64_t)vec_len, stream_),
+        "broadcast_vec");
+}
+
+CudaSlice<bf16> HrmLayerOps::htod_raw_as_bf16(int dtype, const uint8_t* raw, size_t nbytes) const {
+  const size_t size = dtype == HRM_DTYPE_F32 ? 4 : 2;
+  if (dtype != HRM_DTYPE_BF16 && dtype != HRM_DTYPE_F32 && dtype != HRM_DTYPE_F16)
+    fail(HrmError::Kind::InvalidInput, HRM_ERR_DTYPE, "raw_to_bf16: unsupported dtype");
+  if (nbytes % size)
+    fail(HrmError::Kind::InvalidInput, HRM_ERR_INVALID_SHAPE,
+         "raw_to_bf16: " + std::to_string(nbytes) + " bytes is not a whole number of elements");
+  const size_t n = nbytes / size;
+  void* d_raw = nullptr;
+  cuda_check(cudaMalloc(&d_raw, nbytes + (nbytes == 0)), "cudaMalloc");
+  struct Free {
+    void* p;
+    ~Free() { cudaFree(p); }
+  } free_raw{d_raw};
+  cuda_check(cudaMemcpyAsync(d_raw, raw, nbytes, cudaMemcpyHostToDevice, stream_), "cudaMemcpyAsync");
+  CudaSlice<bf16> out = alloc_zero_bf16(n);
+  check(hrm_convert_to_bf16(d_raw, dtype, out.device_ptr(), (int64_t)n, stream_), "raw_to_bf16");
+  cuda_check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");  // before d_raw is freed
+  return out;
+}
+
+std::vector<bf16> HrmLayerOps::raw_to_bf16(int dtype, const std::vector<uint8_t>& raw) const {
+  return sync_reclaim(htod_raw_as_bf16(dtype, raw.data(), raw.size()));
+}
+
 HrmLayerOps::ModuleScratch::ModuleScratch(const HrmLayerOps& ops, size_t rows_)
     : rows(rows_),
       x(ops.alloc_zero_bf16(rows_ * ops.config.hidden_size)),

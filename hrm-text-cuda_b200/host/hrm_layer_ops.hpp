@@ -114,6 +114,25 @@ class HrmLayerOps {
                         CudaSlice<bf16>& output, size_t batch_size, size_t seq_len, size_t hidden_size,
                         size_t vocab_size, float embedding_scale) const;
 
+  // src/lib.rs:505-527: output = sigmoid(gate) * attn_out.
+  void gated_attn_output(const CudaSlice<bf16>& gate, const CudaSlice<bf16>& attn_out, CudaSlice<bf16>& output,
+                         size_t total_elements) const;
+  // src/lib.rs:607-630: attn_out *= sigmoid(gate), in place.
+  void apply_attn_gate(const CudaSlice<bf16>& gate, CudaSlice<bf16>& attn_out, size_t total_elements) const;
+  // src/lib.rs:748-767: dst[r, :] = src for r < n_copies.
+  void broadcast_vec(CudaSlice<bf16>& dst, const CudaSlice<bf16>& src, size_t n_copies, size_t vec_len) const;
+
+  // ---- weight loading (src/lib.rs:1981-2008)
+  // raw_to_bf16: little-endian checkpoint bytes of `dtype` (HRM_DTYPE_BF16 /
+  // F32 / F16) -> bf16 values on the host, as the reference's loader returns
+  // them, converted on the GPU with the same bits (half 2.7.1 rules).  A byte
+  // count that is not a whole number of elements, or another dtype, throws
+  // InvalidInput (the reference asserts or panics).
+  std::vector<bf16> raw_to_bf16(int dtype, const std::vector<uint8_t>& raw) const;
+  // The same conversion into a new device slice, for a loader that keeps the
+  // weights on the GPU (the reference converts on the host, then htod_copy).
+  CudaSlice<bf16> htod_raw_as_bf16(int dtype, const uint8_t* raw, size_t nbytes) const;
+
   // ---- fused entry points that replace wrapper sequences of the reference
   // additive_inject -> rms_norm (src/lib.rs:976-979); weight may be null.
   void add_rms_norm(const CudaSlice<bf16>& x, const CudaSlice<bf16>& branch, CudaSlice<bf16>& residual_out,

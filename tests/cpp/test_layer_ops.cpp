@@ -179,6 +179,70 @@ void test_invalid_input(HrmLayerOps& hrm) {
   expect(thrown, "odd head_dim rejected");
 }
 
+// gated_attn_output / apply_attn_gate with gate = 0 (sigmoid 0.5: exact halves)
+// and broadcast_vec (src/lib.rs:505-527, 607-630, 748-767).
+void test_gates_and_broadcast(HrmLayerOps& hrm) {
+  const size_t n = 1003;  // a vector body and a scalar tail
+  std::vector<float> a(n);
+  for (size_t i = 0; i < n; ++i) a[i] = (float)((int)(i % 37) - 18) * 0.25f;
+  auto gate = hrm.htod_copy_bf16(to_bf16(std::vector<float>(n, 0.0f)));
+  auto attn = hrm.htod_copy_bf16(to_bf16(a));
+  auto out = hrm.alloc_zero_bf16(n);
+  hrm.gated_attn_output(gate, attn, out, n);
+  auto got = hrm.sync_reclaim(std::move(out));
+  for (size_t i = 0; i < n; ++i) expect(got[i].to_f32() == 0.5f * a[i], "gated_attn_output value");
+  hrm.apply_attn_gate(gate, attn, n);
+  auto inplace = hrm.sync_reclaim(std::move(attn));
+  for (size_t i = 0; i < n; ++i) expect(inplace[i].to_f32() == 0.5f * a[i], "apply_attn_gate value");
+
+  const size_t copies = 37, len = 2050;
+  std::vector<float> v(len);
+  for (size_t i = 0; i < len; ++i) v[i] = (float)i - 1000.0f;
+  auto src = hrm.htod_copy_bf16(to_bf16(v));
+  auto dst = hrm.alloc_zero_bf16(copies * len);
+  hrm.broadcast_vec(dst, src, copies, len);
+  auto rows = hrm.sync_reclaim(std::move(dst));
+  const auto want = to_bf16(v);
+  for (size_t r = 0; r < copies; ++r)
+    for (size_t i = 0; i < len; ++i) expect(rows[r * len + i].bits == want[i].bits, "broadcast_vec row");
+}
+
+// raw_to_bf16 (src/lib.rs:1981-2008): f32 rounds to nearest even; a NaN keeps
+// its sign and top payload bits and becomes quiet (half 2.7.1); f16 widens
+// exactly first; bf16 is copied.
+void test_raw_to_bf16(HrmLayerOps& hrm) {
+  auto le = [](std::vector<uint8_t>& out, uint32_t v, int bytes) {
+    for (int b = 0; b < bytes; ++b) out.push_back((uint8_t)(v >> (8 * b)));
+  };
+  std::vector<uint8_t> f32;
+  const uint32_t in32[] = {0x3f800000u, 0xc0200000u, 0x3f808000u, 0x3f818000u, 0x7f800001u, 0xffa00000u, 0x00000001u};
+  const uint16_t out32[] = {0x3f80, 0xc020, 0x3f80, 0x3f82, 0x7fc0, 0xffe0, 0x0000};
+  for (uint32_t v : in32) le(f32, v, 4);
+  auto got = hrm.raw_to_bf16(HRM_DTYPE_F32, f32);
+  expect(got.size() == 7, "f32 count");
+  for (int i = 0; i < 7; ++i) expect(got[i].bits == out32[i], "f32 -> bf16 bits " + std::to_string(i));
+
+  std::vector<uint8_t> f16;
+  const uint16_t in16[] = {0x3c00, 0xc000, 0x0001, 0x7c00, 0x7e01};
+  const uint16_t out16[] = {0x3f80, 0xc000, 0x3380, 0x7f80, 0x7fc0};
+  for (uint16_t v : in16) le(f16, v, 2);
+  got = hrm.raw_to_bf16(HRM_DTYPE_F16, f16);
+  for (int i = 0; i < 5; ++i) expect(got[i].bits == out16[i], "f16 -> bf16 bits " + std::to_string(i));
+
+  std::vector<uint8_t> b16;
+  for (uint16_t v : out32) le(b16, v, 2);
+  got = hrm.raw_to_bf16(HRM_DTYPE_BF16, b16);
+  for (int i = 0; i < 7; ++i) expect(got[i].bits == out32[i], "bf16 copy");
+
+  bool thrown = false;
+  try {
+    hrm.raw_to_bf16(HRM_DTYPE_F32, std::vector<uint8_t>(6));
+  } catch (const HrmError& e) {
+    thrown = e.kind() == HrmError::Kind::InvalidInput;
+  }
+  expect(thrown, "partial element rejected");
+}
+
 // transformer_module (the fused schedule) == the reference's order of wrapper
 // calls and device copies (src/lib.rs:955-1030 per layer, 1036-1105 per module,
 // 1215-1256 per cycle), bit for bit, over 2 H-cycles x 2 L-cycles of 3-layer
@@ -290,6 +354,8 @@ int main() {
       {"test_rope_embed", test_rope_embed},           {"test_add_rms_norm", test_add_rms_norm},
       {"test_split_gqkv_rope", test_split_gqkv_rope},
       {"test_invalid_input", test_invalid_input},
+      {"test_gates_and_broadcast", test_gates_and_broadcast},
+      {"test_raw_to_bf16", test_raw_to_bf16},
       {"test_transformer_module", test_transformer_module},
   };
   try {
