@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(kThreads) convert_scalar_kernel(const uint8_t*
 
 template <int DTYPE>
 cudaError_t launch_dtype(const void* src, void* dst, int64_t n, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   const int64_t cap = (int64_t)device_sm_count() * (2048 / kThreads) * 4;
   int64_t done = 0;
   if (aligned16(src) && aligned16(dst)) {
@@ -97,20 +98,20 @@ cudaError_t launch_dtype(const void* src, void* dst, int64_t n, cudaStream_t s) 
     if (nvec > 0) {
       int64_t blocks = (nvec + kThreads - 1) / kThreads;
       if (blocks > cap) blocks = cap;
-      launch_kernel(convert_vec_kernel<DTYPE>, blocks, kThreads, 0, s, static_cast<const uint4*>(src),
-                                                                      static_cast<uint4*>(dst), nvec);
+      err = launch_kernel(convert_vec_kernel<DTYPE>, blocks, kThreads, 0, s, static_cast<const uint4*>(src),
+          static_cast<uint4*>(dst), nvec);
       done = nvec * 8;
     }
   }
   const int64_t rest = n - done;
-  if (rest > 0) {
+  if (rest > 0 && err == cudaSuccess) {
     constexpr int kSize = DTYPE == HRM_DTYPE_F32 ? 4 : 2;
     int64_t blocks = (rest + kThreads - 1) / kThreads;
     if (blocks > cap) blocks = cap;
-    launch_kernel(convert_scalar_kernel<DTYPE>, blocks, kThreads, 0, s,
+    err = launch_kernel(convert_scalar_kernel<DTYPE>, blocks, kThreads, 0, s,
         static_cast<const uint8_t*>(src) + done * kSize, static_cast<uint16_t*>(dst) + done, rest);
   }
-  return cudaGetLastError();
+  return err;
 }
 
 }  // namespace

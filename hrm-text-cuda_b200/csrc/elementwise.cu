@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(kThreads) ew_scalar_kernel(const uint16_t* a, 
 
 template <class Op>
 cudaError_t launch_ew(const void* a, const void* b, void* out, int64_t n, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   const int64_t max_blocks = (int64_t)device_sm_count() * (2048 / kThreads);
   if (aligned16(a) && aligned16(b) && aligned16(out)) {
     const int64_t nvec = n / 8;
@@ -134,17 +135,15 @@ cudaError_t launch_ew(const void* a, const void* b, void* out, int64_t n, cudaSt
     if (blocks < 1) blocks = 1;
     if (HRM_EW_WAVES > 0 && blocks > max_blocks * HRM_EW_WAVES) blocks = max_blocks * HRM_EW_WAVES;
     if (blocks > INT32_MAX) blocks = INT32_MAX;
-    launch_kernel(ew_vec_kernel<Op>, blocks, kThreads, 0, s, static_cast<const uint4*>(a),
-                                                            static_cast<const uint4*>(b),
-                                                            static_cast<uint4*>(out), nvec, (int)(n % 8));
+    err = launch_kernel(ew_vec_kernel<Op>, blocks, kThreads, 0, s, static_cast<const uint4*>(a),
+        static_cast<const uint4*>(b), static_cast<uint4*>(out), nvec, (int)(n % 8));
   } else {
     int64_t blocks = (n + kThreads - 1) / kThreads;
     if (blocks > max_blocks) blocks = max_blocks;
-    launch_kernel(ew_scalar_kernel<Op>, blocks, kThreads, 0, s, static_cast<const uint16_t*>(a),
-                                                               static_cast<const uint16_t*>(b),
-                                                               static_cast<uint16_t*>(out), n);
+    err = launch_kernel(ew_scalar_kernel<Op>, blocks, kThreads, 0, s, static_cast<const uint16_t*>(a),
+        static_cast<const uint16_t*>(b), static_cast<uint16_t*>(out), n);
   }
-  return cudaGetLastError();
+  return err;
 }
 
 }  // namespace
@@ -162,21 +161,22 @@ cudaError_t launch_attn_gate(const void* gate, const void* attn, void* out, int6
 }
 
 cudaError_t launch_broadcast(void* dst, const void* src, int64_t n_copies, int64_t vec_len, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   const int64_t cap = (int64_t)device_sm_count() * (2048 / kThreads) * 4;
   if (vec_len % 8 == 0 && aligned16(dst) && aligned16(src)) {
     const int64_t chunks = vec_len / 8;
     int64_t blocks = (n_copies * chunks + kThreads - 1) / kThreads;
     if (blocks > cap) blocks = cap;
-    launch_kernel(broadcast_vec_kernel, blocks, kThreads, 0, s, static_cast<uint4*>(dst),
-                                                               static_cast<const uint4*>(src), n_copies, chunks);
+    err = launch_kernel(broadcast_vec_kernel, blocks, kThreads, 0, s, static_cast<uint4*>(dst),
+        static_cast<const uint4*>(src), n_copies, chunks);
   } else {
     int64_t blocks = (n_copies * vec_len + kThreads - 1) / kThreads;
     if (blocks > cap) blocks = cap;
-    launch_kernel(broadcast_scalar_kernel, blocks, kThreads, 0, s, static_cast<uint16_t*>(dst),
-                                                                  static_cast<const uint16_t*>(src), n_copies,
-                                                                  vec_len);
+    err = launch_kernel(broadcast_scalar_kernel, blocks, kThreads, 0, s, static_cast<uint16_t*>(dst),
+        static_cast<const uint16_t*>(src), n_copies,
+        vec_len);
   }
-  return cudaGetLastError();
+  return err;
 }
 
 }  // namespace hrm

@@ -83,22 +83,23 @@ __global__ void __launch_bounds__(kThreads) embedding_scalar_kernel(const uint32
 
 cudaError_t launch_embedding(const uint32_t* ids, const void* table, void* out, int64_t tokens, int64_t hidden,
                              int64_t vocab, float scale, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   const int64_t wave = (int64_t)device_sm_count() * (2048 / kThreads);
   if (hidden % 8 == 0 && hidden / 8 <= INT32_MAX && aligned16(table) && aligned16(out)) {
     int64_t blocks = (tokens + kWarps - 1) / kWarps;
     if (HRM_EMB_WAVES > 0 && blocks > wave * HRM_EMB_WAVES) blocks = wave * HRM_EMB_WAVES;
     if (blocks > INT32_MAX) blocks = INT32_MAX;
-    launch_kernel(embedding_warp_kernel, blocks, kThreads, 0, s, ids, static_cast<const uint4*>(table),
-                                                                 static_cast<uint4*>(out), tokens,
-                                                                 (int)(hidden / 8), (uint32_t)vocab, scale);
+    err = launch_kernel(embedding_warp_kernel, blocks, kThreads, 0, s, ids, static_cast<const uint4*>(table),
+        static_cast<uint4*>(out), tokens,
+        (int)(hidden / 8), (uint32_t)vocab, scale);
   } else {
     int64_t blocks = (tokens * hidden + kThreads - 1) / kThreads;
     if (blocks > wave) blocks = wave;
-    launch_kernel(embedding_scalar_kernel, blocks, kThreads, 0, s, ids, static_cast<const uint16_t*>(table),
-                                                                   static_cast<uint16_t*>(out), tokens, hidden,
-                                                                   (uint32_t)vocab, scale);
+    err = launch_kernel(embedding_scalar_kernel, blocks, kThreads, 0, s, ids, static_cast<const uint16_t*>(table),
+        static_cast<uint16_t*>(out), tokens, hidden,
+        (uint32_t)vocab, scale);
   }
-  return cudaGetLastError();
+  return err;
 }
 
 }  // namespace hrm

@@ -22,11 +22,12 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // stream s.  The launch is programmatic (cudaLaunchAttributeProgrammatic-
 // StreamSerialization): it may start before the previous kernel in s has
 // finished, which is safe because every kernel of this library waits for that
-// kernel at its entry (grid_dependency_begin).  Errors are left for
-// cudaGetLastError, as a triple-chevron launch leaves them.
+// kernel at its entry (grid_dependency_begin).  Returns the launch's own
+// status, so an error left pending by an earlier, unrelated call is neither
+// reported as this launch's nor cleared.
 template <typename... KArgs, typename... Args>
-inline void launch_kernel(void (*k)(KArgs...), int64_t grid, int block, size_t smem, cudaStream_t s,
-                          Args&&... args) {
+inline cudaError_t launch_kernel(void (*k)(KArgs...), int64_t grid, int block, size_t smem, cudaStream_t s,
+                                 Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3((unsigned)block);
@@ -37,7 +38,7 @@ inline void launch_kernel(void (*k)(KArgs...), int64_t grid, int block, size_t s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = HRM_PDL ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, k, static_cast<Args&&>(args)...);
+  return cudaLaunchKernelEx(&cfg, k, static_cast<Args&&>(args)...);
 }
 
 cudaError_t launch_additive_inject(const void* a, const void* b, void* out, int64_t n, cudaStream_t s);

@@ -369,6 +369,7 @@ int pow2_ceil(int64_t x) {
 
 cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                         int64_t offset, float theta, const float* table, bool token_major, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   const int64_t sms = device_sm_count();
   const int g = (int)(head_dim / 16);
   const bool fast = head_dim % 16 == 0 && head_dim <= 512 && (g & (g - 1)) == 0 && aligned16(q) &&
@@ -398,32 +399,33 @@ cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t 
     if (HRM_ROPE_CAP > 0 && blocks > sms * HRM_ROPE_CAP) blocks = sms * HRM_ROPE_CAP;
     if (blocks > INT32_MAX) blocks = INT32_MAX;
     if (table != nullptr)
-      launch_kernel(rope_tile_kernel<true>, blocks, kThreads, 0, s, a);
+      err = launch_kernel(rope_tile_kernel<true>, blocks, kThreads, 0, s, a);
     else
-      launch_kernel(rope_tile_kernel<false>, blocks, kThreads, 0, s, a);
+      err = launch_kernel(rope_tile_kernel<false>, blocks, kThreads, 0, s, a);
   } else {
     const int64_t rows = batch * heads * seq;
     int64_t blocks = (rows * (head_dim / 2) + 255) / 256;
     if (blocks > sms * 8) blocks = sms * 8;
-    launch_kernel(rope_scalar_kernel, blocks, 256, 0, s, static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), rows,
-                                                        seq, token_major ? heads : 1, (int)head_dim, (int)offset,
-                                                        theta, table);
+    err = launch_kernel(rope_scalar_kernel, blocks, 256, 0, s, static_cast<uint16_t*>(q), static_cast<uint16_t*>(k),
+        rows, seq, token_major ? heads : 1, (int)head_dim, (int)offset, theta, table);
   }
-  return cudaGetLastError();
+  return err;
 }
 
 cudaError_t launch_rope_table(float* table, int64_t positions, int64_t head_dim, float theta, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   int64_t blocks = (positions * (head_dim / 2) + 255) / 256;
   const int64_t cap = (int64_t)device_sm_count() * 8;
   if (blocks > cap) blocks = cap;
-  launch_kernel(rope_table_kernel, blocks, 256, 0, s, table, positions, (int)head_dim, theta);
-  return cudaGetLastError();
+  err = launch_kernel(rope_table_kernel, blocks, 256, 0, s, table, positions, (int)head_dim, theta);
+  return err;
 }
 
 cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, void* v, void* kc, void* vc,
                               int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t offset,
                               float theta, const float* table, int64_t cache_len, int64_t cache_offset,
                               cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   const int64_t sms = device_sm_count();
   const int g = (int)(head_dim / 16);
   const bool fast = head_dim % 16 == 0 && head_dim <= 512 && (g & (g - 1)) == 0 && aligned16(gqkv) &&
@@ -458,24 +460,24 @@ cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, vo
     if (blocks > INT32_MAX) blocks = INT32_MAX;
     if (table != nullptr) {
       if (kc != nullptr)
-        launch_kernel(split_rope_tile_kernel<true, true>, blocks, kThreads, 0, s, a);
+        err = launch_kernel(split_rope_tile_kernel<true, true>, blocks, kThreads, 0, s, a);
       else
-        launch_kernel(split_rope_tile_kernel<true, false>, blocks, kThreads, 0, s, a);
+        err = launch_kernel(split_rope_tile_kernel<true, false>, blocks, kThreads, 0, s, a);
     } else {
       if (kc != nullptr)
-        launch_kernel(split_rope_tile_kernel<false, true>, blocks, kThreads, 0, s, a);
+        err = launch_kernel(split_rope_tile_kernel<false, true>, blocks, kThreads, 0, s, a);
       else
-        launch_kernel(split_rope_tile_kernel<false, false>, blocks, kThreads, 0, s, a);
+        err = launch_kernel(split_rope_tile_kernel<false, false>, blocks, kThreads, 0, s, a);
     }
   } else {
     int64_t blocks = (batch * heads * seq * (head_dim / 2) + 255) / 256;
     if (blocks > sms * 8) blocks = sms * 8;
-    launch_kernel(split_rope_scalar_kernel, blocks, 256, 0, s,
+    err = launch_kernel(split_rope_scalar_kernel, blocks, 256, 0, s,
         static_cast<const uint16_t*>(gqkv), static_cast<uint16_t*>(gate), static_cast<uint16_t*>(q),
         static_cast<uint16_t*>(k), static_cast<uint16_t*>(v), static_cast<uint16_t*>(kc), static_cast<uint16_t*>(vc),
         batch, seq, (int)heads, (int)head_dim, (int)offset, theta, table, cache_len, cache_offset);
   }
-  return cudaGetLastError();
+  return err;
 }
 
 }  // namespace hrm

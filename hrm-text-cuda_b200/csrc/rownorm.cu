@@ -549,6 +549,7 @@ int resident_ctas(K kernel, size_t smem) {
 
 template <int VPL, int MODE, bool HAS_W>
 cudaError_t launch_warp_on(const RowArgs& a, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   auto kernel = rownorm_warp_kernel<VPL, MODE, HAS_W>;
   static std::atomic<int> occ{0};  // resident CTAs per SM (smem <= 8 KB never limits it)
   int o = occ.load(std::memory_order_relaxed);
@@ -561,8 +562,8 @@ cudaError_t launch_warp_on(const RowArgs& a, cudaStream_t s) {
   const int64_t wave = (int64_t)device_sm_count() * o;
   if (HRM_RN_WAVES > 0 && blocks > wave * HRM_RN_WAVES) blocks = wave * HRM_RN_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;
-  launch_kernel(kernel, blocks, kThreads, smem, s, a);
-  return cudaGetLastError();
+  err = launch_kernel(kernel, blocks, kThreads, smem, s, a);
+  return err;
 }
 
 template <int MODE, bool HAS_W>
@@ -611,6 +612,7 @@ int bulk_plan(int nchunks, int rows_per_stage, bool has_w, size_t* smem) {
 
 template <int VPL, int MODE, bool HAS_W>
 cudaError_t launch_bulk_on(const RowArgs& a, int nwarps, size_t smem, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   auto kernel = rownorm_bulk_kernel<VPL, MODE, HAS_W>;
   static std::atomic<bool> opted[64];  // per device: the opt-in is per function and device
   int dev = 0;
@@ -630,8 +632,8 @@ cudaError_t launch_bulk_on(const RowArgs& a, int nwarps, size_t smem, cudaStream
     if (blocks > sms) blocks = sms;  // one CTA per SM, warps loop over their rows
   }
   if (blocks > INT32_MAX) blocks = INT32_MAX;
-  launch_kernel(kernel, blocks, 32 * nwarps, smem, s, a);
-  return cudaGetLastError();
+  err = launch_kernel(kernel, blocks, 32 * nwarps, smem, s, a);
+  return err;
 }
 
 template <int MODE, bool HAS_W>
@@ -649,11 +651,12 @@ cudaError_t dispatch_bulk(const RowArgs& a, int nwarps, size_t smem, cudaStream_
 
 template <typename T, int MODE, bool HAS_W>
 cudaError_t launch_block(const RowArgsScalar& a, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   int64_t blocks = a.rows;
   const int64_t cap = (int64_t)device_sm_count() * 64;
   if (blocks > cap) blocks = cap;
-  launch_kernel(rownorm_block_kernel<T, MODE, HAS_W>, blocks, kBlockThreads, 0, s, a);
-  return cudaGetLastError();
+  err = launch_kernel(rownorm_block_kernel<T, MODE, HAS_W>, blocks, kBlockThreads, 0, s, a);
+  return err;
 }
 
 template <int MODE>
@@ -701,6 +704,7 @@ cudaError_t launch_bf16_rows(const void* x, const void* b, const uint32_t* ids, 
 
 template <int VPL, bool HAS_W>
 cudaError_t launch_f32_warp(const RowArgsF32& a, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
   auto kernel = rms_f32_warp_kernel<VPL, HAS_W>;
   static std::atomic<int> occ{0};
   int o = occ.load(std::memory_order_relaxed);
@@ -713,8 +717,8 @@ cudaError_t launch_f32_warp(const RowArgsF32& a, cudaStream_t s) {
   const int64_t wave = (int64_t)device_sm_count() * o;
   if (HRM_RN_WAVES > 0 && blocks > wave * HRM_RN_WAVES) blocks = wave * HRM_RN_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;
-  launch_kernel(kernel, blocks, kThreads, smem, s, a);
-  return cudaGetLastError();
+  err = launch_kernel(kernel, blocks, kThreads, smem, s, a);
+  return err;
 }
 
 template <bool HAS_W>

@@ -243,6 +243,19 @@ void test_raw_to_bf16(HrmLayerOps& hrm) {
   expect(thrown, "partial element rejected");
 }
 
+// An error the caller left pending (a failed allocation) is neither reported
+// as a layer-op failure nor cleared: each launch returns its own status.
+void test_pending_error_not_claimed(HrmLayerOps& hrm) {
+  auto a = hrm.htod_copy_bf16(to_bf16({1.0f, 2.0f, 3.0f, 4.0f}));
+  auto out = hrm.alloc_zero_bf16(4);
+  void* huge = nullptr;
+  expect(cudaMalloc(&huge, (size_t)1 << 62) != cudaSuccess, "the oversized allocation fails");
+  hrm.additive_inject(a, a, out, 4);  // must not throw
+  expect(cudaGetLastError() == cudaErrorMemoryAllocation, "the caller's error is still pending");
+  auto host = hrm.sync_reclaim(std::move(out));
+  expect(host[3].to_f32() == 8.0f, "additive_inject value");
+}
+
 // transformer_module (the fused schedule) == the reference's order of wrapper
 // calls and device copies (src/lib.rs:955-1030 per layer, 1036-1105 per module,
 // 1215-1256 per cycle), bit for bit, over 2 H-cycles x 2 L-cycles of 3-layer
@@ -355,6 +368,7 @@ int main() {
       {"test_split_gqkv_rope", test_split_gqkv_rope},
       {"test_invalid_input", test_invalid_input},
       {"test_gates_and_broadcast", test_gates_and_broadcast},
+      {"test_pending_error_not_claimed", test_pending_error_not_claimed},
       {"test_raw_to_bf16", test_raw_to_bf16},
       {"test_transformer_module", test_transformer_module},
   };
