@@ -26,6 +26,11 @@ reads back from additive_inject's output.
 Per token and layer the residual stream moves 16 * hidden bytes here (two
 fused calls of 8 * hidden) against 28 * hidden in the reference's order (two
 norms, two adds, two copies), plus SwiGLU's 6 * intermediate in both.
+
+recurrent_forward runs the loop around the modules (src/lib.rs:1189-1270):
+z_H from the embedding, z_L broadcast from z_l_init, then per H-cycle
+l_cycles x z_L = L(z_L + z_H) and z_H = H(z_H + z_L), with the reference's
+KV-cache slot numbering.
 """
 
 from __future__ import annotations
@@ -35,7 +40,7 @@ from typing import Callable, Optional, Sequence
 
 import torch
 
-from .ops import add_rms_norm, swiglu_ffn
+from .ops import add_rms_norm, broadcast_vec, embedding_lookup, swiglu_ffn
 
 # attention(layer, normed [rows, H], out [rows, H])
 AttentionFn = Callable[[int, torch.Tensor, torch.Tensor], None]
@@ -125,3 +130,54 @@ def reference_order_bytes_per_token(hidden: int, intermediate: int, n_layers: in
     (4H); the final norm (4H) and its copy (4H)."""
     return (10 * hidden + n_layers * (24 * hidden + 6 * intermediate) + (n_layers - 1) * 4 * hidden
             + 8 * hidden)
+
+
+# attention(layer, kv_slot, normed [rows, H], out [rows, H]) of recurrent_forward
+SlotAttentionFn = Callable[[int, int, torch.Tensor, torch.Tensor], None]
+
+
+@dataclass
+class ModuleFns:
+    """One module (H or L) for recurrent_forward: its layer count, the caller's
+    attention (given the layer and the KV-cache slot) and FFN GEMMs, and
+    optional norm weights."""
+
+    n_layers: int
+    attention: SlotAttentionFn
+    gate_up: GateUpFn
+    down: DownFn
+    norms: Optional[ModuleNorms] = None
+
+
+def recurrent_forward(input_ids: torch.Tensor, embed_table: torch.Tensor, embedding_scale: float,
+                      z_l_init: torch.Tensor, h_cycles: int, l_cycles: int, l_module: ModuleFns,
+                      h_module: ModuleFns, scratch: ModuleScratch, *, eps: float = 1e-6,
+                      z_h: Optional[torch.Tensor] = None, z_l: Optional[torch.Tensor] = None, stream=None):
+    """(z_H, z_L) after the HRM recurrent loop over `input_ids` (rows tokens).
+
+    src/lib.rs:1189-1270: z_H = embedding_lookup(ids) * scale (1189-1200);
+    z_L = broadcast(z_l_init) (1202-1203); then for each of h_cycles:
+    l_cycles times z_L = L(z_L + z_H), then z_H = H(z_H + z_L), every module
+    pass through transformer_module.  KV-cache slots are numbered as the
+    reference's kv_slot_counter: each module pass takes the next n_layers slots,
+    and its attention sees slot = base + layer.  The LM head, sampling and the
+    cache itself stay with the caller.
+    """
+    rows, hidden = scratch.rows, scratch.hidden
+    if input_ids.numel() != rows:
+        raise ValueError(f"{input_ids.numel()} token ids for a scratch of {rows} rows")
+    z_h = embedding_lookup(input_ids.reshape(-1), embed_table, embedding_scale, out=z_h, stream=stream)
+    z_l = broadcast_vec(z_l_init.reshape(-1), rows, out=z_l, stream=stream)
+    slot = 0
+
+    def run(m: ModuleFns, z_a: torch.Tensor, z_b: torch.Tensor, base: int) -> None:
+        transformer_module(z_a, z_b, z_a, m.n_layers, lambda i, n, o: m.attention(i, base + i, n, o), m.gate_up,
+                           m.down, scratch, eps=eps, norms=m.norms, stream=stream)
+
+    for _ in range(h_cycles):
+        for _ in range(l_cycles):
+            run(l_module, z_l, z_h, slot)
+            slot += l_module.n_layers
+        run(h_module, z_h, z_l, slot)
+        slot += h_module.n_layers
+    return z_h.view(rows, hidden), z_l.view(rows, hidden)

@@ -17,7 +17,7 @@ import pytest
 import torch
 
 import hrm_layer_ops as ops
-from hrm_layer_ops.module import ModuleNorms, ModuleScratch, transformer_module
+from hrm_layer_ops.module import ModuleFns, ModuleNorms, ModuleScratch, recurrent_forward, transformer_module
 from helpers import assert_bits_equal, normal_bf16, to_dev, to_host
 
 pytestmark = pytest.mark.gpu
@@ -108,6 +108,40 @@ def test_recurrent_loop_matches_oracle_in_reference_order(oracle, cuda):
         z_h = _oracle_module(oracle, z_h, z_l, L, hs, EPS)
     assert_bits_equal(to_host(dl), z_l, "z_L")
     assert_bits_equal(to_host(dh), z_h, "z_H")
+
+
+def test_recurrent_forward_matches_oracle_in_reference_order(oracle, cuda):
+    """The whole loop of src/lib.rs:1189-1270 -- embedding into z_H, z_L
+    broadcast from z_l_init, 2 H-cycles x 3 L-cycles of 2-layer modules -- equals
+    the oracle running the reference's order, and the attention callbacks see
+    the reference's KV-slot numbering (each module pass takes the next
+    n_layers slots)."""
+    rows, H, I, L, V = 48, 256, 704, 2, 100
+    scale = 16.0
+    rng = np.random.default_rng(23)
+    ids = rng.integers(0, V + 3, rows, dtype=np.uint32)          # a few out of range: clamped
+    table = normal_bf16(rng, (V, H), 0.5)
+    z_l_init = normal_bf16(rng, H)
+    sa = ExactStandIns(H, I, cuda)
+    seen = []
+
+    def attention(i, slot, n, out):
+        seen.append(slot)
+        sa.attention(i, n, out)
+
+    m = ModuleFns(L, attention, sa.gate_up, sa.down)
+    z_h, z_l = recurrent_forward(to_dev(ids, cuda), to_dev(table, cuda), scale, to_dev(z_l_init, cuda), 2, 3, m, m,
+                                 ModuleScratch(rows, H, I, cuda), eps=EPS)
+    hs = _host_standins(H, I)
+    wh = oracle.embedding_lookup(ids, table, scale)
+    wl = oracle.broadcast_vec(z_l_init, rows)
+    for _ in range(2):
+        for _ in range(3):
+            wl = _oracle_module(oracle, wl, wh, L, hs, EPS)
+        wh = _oracle_module(oracle, wh, wl, L, hs, EPS)
+    assert_bits_equal(to_host(z_h), wh.reshape(rows, H), "z_H")
+    assert_bits_equal(to_host(z_l), wl.reshape(rows, H), "z_L")
+    assert seen == list(range(2 * (3 + 1) * L))
 
 
 # --------------------------------------------------- GEMM stand-ins (cuBLAS)
