@@ -213,14 +213,16 @@ enum hrm_dtype { HRM_DTYPE_BF16 = 0, HRM_DTYPE_F32 = 1, HRM_DTYPE_F16 = 2 };
  * GPU.  dst must not overlap src.                                           */
 int hrm_convert_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, hrm_stream_t stream);
 
-/* Number of bounded device-side waits that ran out since the library was
- * loaded (or since the last reset).  The bulk-copy kernels wait on mbarriers
- * with a deadline of about one second; a wait that runs out counts itself
- * here and the kernel returns instead of hanging, leaving the affected rows
- * unwritten.  It reads device memory: call it after synchronizing the streams
- * that ran the library's kernels.  0 in correct operation.  reset != 0 sets
- * the count back to 0 after reading it.  No reference counterpart (the
- * reference's kernels have no waits).                                       */
+/* Number of bounded device-side waits that ran out on the current device
+ * since the library was loaded there (or since the last reset).  The
+ * bulk-copy kernels of the opt-in build wait on mbarriers with a deadline of
+ * about one second; a wait that runs out counts itself here and the kernel
+ * returns instead of hanging, leaving the affected rows unwritten.  It reads
+ * device memory: call it after synchronizing the streams that ran the
+ * library's kernels.  0 in correct operation (and always 0 in the default
+ * build, which has no waits).  reset != 0 sets the count back to 0 after
+ * reading it.  No reference counterpart (the reference's kernels have no
+ * waits).                                                                   */
 int hrm_wait_timeouts(unsigned int* count, int reset);
 
 #ifdef __cplusplus
