@@ -51,6 +51,22 @@ def test_python_front_end_binds_every_declared_symbol():
     assert declared == set(_lib.SIGNATURES)
 
 
+def declared_arity():
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(hrm_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        out[m.group(1)] = len([a for a in m.group(2).split(",") if a.strip() and a.strip() != "void"])
+    return out
+
+
+def test_python_bindings_match_header_arity():
+    from hrm_layer_ops import _lib
+
+    arity = declared_arity()
+    for name, args in _lib.SIGNATURES.items():
+        assert len(args) == arity[name], (name, len(args), arity[name])
+
+
 def test_static_archive_and_cpp_host_built():
     for f in ("lib/libhrm_ops.a", "lib/libhrm_host.a", "build/test_layer_ops", "build/test_wait_timeout"):
         assert os.path.exists(os.path.join(PKG, f)), f
