@@ -2,8 +2,8 @@
 """Throughput benchmark of the sm_100a per-token layer operators.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload chain|add_rms_norm|rms_norm_f32|rope|swiglu|embedding|split_rope|
-                                attn_gate|convert_f32|module]
+                    [--workload chain|add_rms_norm|rms_norm_f32|rms_norm|rope|swiglu|embedding|
+                                split_rope|attn_gate|convert_f32|module]
 
 Default workload ("chain"): the chained layer-op pass on 65536 tokens per GPU
 -- embedding [32000 x 2048] ~ N(0, 0.02) gathered for ids ~ U[0, 32000) and
@@ -65,8 +65,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="chain",
-                    choices=["chain", "add_rms_norm", "rms_norm_f32", "rope", "swiglu", "embedding", "split_rope",
-                             "attn_gate", "convert_f32", "module"])
+                    choices=["chain", "add_rms_norm", "rms_norm_f32", "rms_norm", "rope", "swiglu", "embedding",
+                             "split_rope", "attn_gate", "convert_f32", "module"])
     ap.add_argument("--tokens", type=int, default=CHAIN_B * CHAIN_S,
                     help="chain tokens per GPU (a multiple of 4096; default 65536)")
     ap.add_argument("--qk-layout", choices=["token", "head"], default="token",
@@ -369,6 +369,12 @@ class SingleOp:
             mk = lambda: (torch.randn((R, HIDDEN), generator=gen, device=device),
                           torch.empty((R, HIDDEN), device=device))
             self.cfg = {"workload": "RMSNorm fp32 [4096 x 2048]", "rows": R}
+        elif name == "rms_norm":          # [4096 x 2048] bf16, weight, eps 1e-5
+            R = 4096
+            self.w = randn_bf16(HIDDEN, gen, device, 0.1, 1.0)
+            self.bytes_per_step, self.rows_per_step = R * HIDDEN * 4, R
+            mk = lambda: (randn_bf16((R, HIDDEN), gen, device), torch.empty((R, HIDDEN), dtype=bf, device=device))
+            self.cfg = {"workload": "RMSNorm bf16 [4096 x 2048]", "rows": R}
         elif name == "rope":              # Q, K [8, 16, 4096, 128], table
             shape = (8, HEADS, 4096, HEAD_DIM)
             self.table = ops.rope_table(4096, HEAD_DIM, THETA, device)
@@ -430,7 +436,7 @@ class SingleOp:
             events[0].record(stream)
         if self.name == "add_rms_norm":
             ops.add_rms_norm(b[0], b[1], self.w, EPS, residual_out=b[2], normed_out=b[3], stream=stream)
-        elif self.name == "rms_norm_f32":
+        elif self.name in ("rms_norm_f32", "rms_norm"):
             ops.rms_norm(b[0], self.w, EPS, out=b[1], stream=stream)
         elif self.name == "rope":
             ops.rope_embed(b[0], b[1], 0, THETA, self.table, stream=stream)
@@ -452,7 +458,7 @@ class SingleOp:
         """Per step: H2D of the inputs from pinned host memory, the kernel, D2H of the outputs."""
         torch = self.torch
         b = self.bufs[0]
-        n_in = {"add_rms_norm": 2, "rms_norm_f32": 1, "rope": 2, "swiglu": 2, "embedding": 1,
+        n_in = {"add_rms_norm": 2, "rms_norm_f32": 1, "rms_norm": 1, "rope": 2, "swiglu": 2, "embedding": 1,
                 "split_rope": 1, "attn_gate": 2, "convert_f32": 1}[self.name]
         outs = {"rope": [0, 1], "attn_gate": [1]}.get(self.name, list(range(n_in, len(b))))
         host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in b]

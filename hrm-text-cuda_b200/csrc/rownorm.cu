@@ -36,15 +36,25 @@ namespace {
 // Launch shape of the warp-per-row kernels (compile-time; defaults tuned):
 //   HRM_RN_WARPS      warps per CTA
 //   HRM_RN_WAVES      grid cap in waves of resident CTAs (0: one warp per row)
-//   HRM_RN_MINBLOCKS  __launch_bounds__ minimum resident CTAs per SM
+//   HRM_RN_MINBLOCKS  __launch_bounds__ minimum resident CTAs per SM (2: at most
+//                     128 registers, which keeps embed + RMSNorm at 3 CTAs per
+//                     SM and the fp32 kernel at 2 with no spills)
 #ifndef HRM_RN_WARPS
 #define HRM_RN_WARPS 8
 #endif
 #ifndef HRM_RN_WAVES
 #define HRM_RN_WAVES 0
 #endif
+// Grid cap of the fp32 kernel, in waves (0: one warp per row), and its
+// __launch_bounds__ minimum resident CTAs per SM.
+#ifndef HRM_RN_F32_WAVES
+#define HRM_RN_F32_WAVES HRM_RN_WAVES
+#endif
+#ifndef HRM_RN_F32_MINBLOCKS
+#define HRM_RN_F32_MINBLOCKS HRM_RN_MINBLOCKS
+#endif
 #ifndef HRM_RN_MINBLOCKS
-#define HRM_RN_MINBLOCKS 1
+#define HRM_RN_MINBLOCKS 2
 #endif
 
 constexpr int kWarps = HRM_RN_WARPS;          // warp-per-row kernels
@@ -163,31 +173,50 @@ __device__ __forceinline__ void accum8(float (&p)[8], const uint4& v) {
   }
 }
 
-// Stages `nchunks` 16-byte chunks of w into shared memory (whole CTA).
-__device__ __forceinline__ void stage_weight(uint4* s_w, const uint4* w, int nchunks) {
+// ------------------------------------------------------------ bf16 fast path
+// Weight staging.  The CTA's cp.async copies of the weight stay in flight while
+// its warps load and reduce their first rows; the CTA waits for them (and
+// publishes them with a barrier) only before the first normalisation, so a CTA
+// start does not serialise a weight fetch before its row loads.  Every warp
+// runs the first iteration of the row loop -- a warp without a row does no
+// memory work -- so that all threads reach that barrier.
+__device__ __forceinline__ void issue_weight(uint4* s_w, const uint4* w, int nchunks) {
   for (int c = threadIdx.x; c < nchunks; c += kThreads) cp_async16(&s_w[c], w + c);
   cp_async_commit();
+}
+__device__ __forceinline__ void publish_weight() {
   cp_async_wait_all();
   __syncthreads();
 }
 
-// ------------------------------------------------------------ bf16 fast path
+// Minimum resident CTAs: HRM_RN_MINBLOCKS (<= 128 registers per thread), except
+// add + RMSNorm over rows of more than 2048 elements, whose x and branch chunks
+// (2 x 16 per lane) need more registers than that without spilling.
+template <int VPL, int MODE>
+constexpr int rownorm_min_blocks() {
+  return (MODE == kAdd && VPL > 8) ? 1 : HRM_RN_MINBLOCKS;
+}
+
 template <int VPL, int MODE, bool HAS_W>
-__global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rownorm_warp_kernel(const RowArgs a) {
+__global__ void __launch_bounds__(kThreads, rownorm_min_blocks<VPL, MODE>()) rownorm_warp_kernel(const RowArgs a) {
   grid_dependency_begin();
   extern __shared__ uint4 s_w[];
   const int lane = threadIdx.x & 31;
-  if (HAS_W) stage_weight(s_w, a.w, a.nchunks);
+  if (HAS_W) issue_weight(s_w, a.w, a.nchunks);
 
   const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
-  for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < a.rows; row += warp_stride) {
-    const uint4* src;
-    if (MODE == kEmbed) {
-      uint32_t id = a.ids[row];
-      if (id >= a.vocab) id = a.vocab - 1;  // src/kernels/embedding_lookup.cu:35
-      src = a.x + (int64_t)id * a.nchunks;
-    } else {
-      src = a.x + row * a.nchunks;
+  int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  for (bool first = true; first || row < a.rows; first = false, row += warp_stride) {
+    const bool active = row < a.rows;  // uniform across the warp
+    const uint4* src = a.x;
+    if (active) {
+      if (MODE == kEmbed) {
+        uint32_t id = a.ids[row];
+        if (id >= a.vocab) id = a.vocab - 1;  // src/kernels/embedding_lookup.cu:35
+        src = a.x + (int64_t)id * a.nchunks;
+      } else {
+        src = a.x + row * a.nchunks;
+      }
     }
     const int64_t base = row * a.nchunks;
 
@@ -197,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rownorm_warp_kerne
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int c = lane + 32 * j;
-      if (c < a.nchunks) {
+      if (active && c < a.nchunks) {
         if (MODE == kEmbed) {
           v[j] = ld_keep(src + c);  // table rows may repeat: keep them in L2
         } else {
@@ -212,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rownorm_warp_kerne
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int c = lane + 32 * j;
-      if (c < a.nchunks) {
+      if (active && c < a.nchunks) {
         if (MODE == kAdd) {
           v[j] = add8(v[j], vb[j]);
           st_stream(a.r + base + c, v[j]);
@@ -224,10 +253,11 @@ __global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rownorm_warp_kerne
       }
     }
     const float inv = inv_rms(ref_tree_bf16(p), a.hidden, a.eps);
+    if (HAS_W && first) publish_weight();
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int c = lane + 32 * j;
-      if (c < a.nchunks) {
+      if (active && c < a.nchunks) {
         uint4 wv = make_uint4(0, 0, 0, 0);
         if (HAS_W) wv = s_w[c];
         st_stream(a.y + base + c, norm8<HAS_W>(v[j], inv, wv));
@@ -402,27 +432,29 @@ struct RowArgsF32 {
 };
 
 template <int VPL, bool HAS_W>
-__global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rms_f32_warp_kernel(const RowArgsF32 a) {
+__global__ void __launch_bounds__(kThreads, HRM_RN_F32_MINBLOCKS) rms_f32_warp_kernel(const RowArgsF32 a) {
   grid_dependency_begin();
   extern __shared__ uint4 s_w4[];
   float4* s_w = reinterpret_cast<float4*>(s_w4);
   const int lane = threadIdx.x & 31;
-  if (HAS_W) stage_weight(s_w4, reinterpret_cast<const uint4*>(a.w), a.nchunks);
+  if (HAS_W) issue_weight(s_w4, reinterpret_cast<const uint4*>(a.w), a.nchunks);
 
   const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
-  for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < a.rows; row += warp_stride) {
+  int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  for (bool first = true; first || row < a.rows; first = false, row += warp_stride) {
+    const bool active = row < a.rows;  // uniform across the warp
     const int64_t base = row * a.nchunks;
     float4 v[VPL];
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int c = lane + 32 * j;
-      if (c < a.nchunks) v[j] = __ldcs(a.x + base + c);
+      if (active && c < a.nchunks) v[j] = __ldcs(a.x + base + c);
     }
     float pa[4] = {0.f, 0.f, 0.f, 0.f}, pc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int c = lane + 32 * j;
-      if (c < a.nchunks) {
+      if (active && c < a.nchunks) {
         float(&p)[4] = (j & 1) ? pc : pa;
         p[0] = fmaf(v[j].x, v[j].x, p[0]);
         p[1] = fmaf(v[j].y, v[j].y, p[1]);
@@ -431,10 +463,11 @@ __global__ void __launch_bounds__(kThreads, HRM_RN_MINBLOCKS) rms_f32_warp_kerne
       }
     }
     const float inv = inv_rms(ref_tree_f32(pa, pc), a.hidden, a.eps);
+    if (HAS_W && first) publish_weight();
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int c = lane + 32 * j;
-      if (c < a.nchunks) {
+      if (active && c < a.nchunks) {
         float4 o = make_float4(v[j].x * inv, v[j].y * inv, v[j].z * inv, v[j].w * inv);
         if (HAS_W) {
           const float4 wv = s_w[c];
@@ -715,7 +748,7 @@ cudaError_t launch_f32_warp(const RowArgsF32& a, cudaStream_t s) {
   const size_t smem = HAS_W ? (size_t)a.nchunks * 16 : 0;
   int64_t blocks = (a.rows + kWarps - 1) / kWarps;
   const int64_t wave = (int64_t)device_sm_count() * o;
-  if (HRM_RN_WAVES > 0 && blocks > wave * HRM_RN_WAVES) blocks = wave * HRM_RN_WAVES;
+  if (HRM_RN_F32_WAVES > 0 && blocks > wave * HRM_RN_F32_WAVES) blocks = wave * HRM_RN_F32_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;
   err = launch_kernel(kernel, blocks, kThreads, smem, s, a);
   return err;
