@@ -28,6 +28,22 @@ def test_rms_norm_f32_4096x2048(oracle, cuda):
     assert np.array_equal(y.view(np.uint32), oracle.rms_norm_f32(x, w, eps=1e-5).view(np.uint32))
 
 
+@pytest.mark.parametrize("dtype,rows", [("bf16", 4096), ("bf16", 16384), ("f32", 4096), ("f32", 8192)])
+def test_rms_norm_both_paths(oracle, cuda, dtype, rows):
+    """Plain RMSNorm [rows x 2048] with a weight at the benchmark's row count
+    and at 2-4x more (several waves of CTAs per SM), bit-exact."""
+    rng = np.random.default_rng(rows)
+    if dtype == "f32":
+        x = rng.standard_normal((rows, 2048)).astype(np.float32)
+        w = (1 + 0.1 * rng.standard_normal(2048)).astype(np.float32)
+        y = ops.rms_norm(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), eps=1e-5).cpu().numpy()
+        assert np.array_equal(y.view(np.uint32), oracle.rms_norm_f32(x, w, eps=1e-5).view(np.uint32))
+    else:
+        x, w = normal_bf16(rng, (rows, 2048), 1.5), normal_bf16(rng, 2048, 0.1, 1.0)
+        y = ops.rms_norm(to_dev(x, cuda), to_dev(w, cuda), eps=1e-5)
+        assert_bits_equal(to_host(y), oracle.rms_norm(x, w, eps=1e-5), f"bf16 {rows} rows")
+
+
 def test_add_rms_norm_16384x2048(oracle, cuda):
     """Fused residual add + RMSNorm bf16 [16384 x 2048], w = 1 + 0.1 N(0,1), eps 1e-5."""
     rng = np.random.default_rng(1)
