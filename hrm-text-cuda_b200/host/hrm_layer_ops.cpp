@@ -310,4 +310,30 @@ void HrmLayerOps::transformer_module(const CudaSlice<bf16>& z_a, const CudaSlice
   }
 }
 
+void HrmLayerOps::recurrent_forward(const CudaSlice<uint32_t>& input_ids, const CudaSlice<bf16>& embed_table,
+                                    size_t vocab_size, const CudaSlice<bf16>& z_l_init, size_t h_cycles,
+                                    size_t l_cycles, const ModuleCallbacks& l_module,
+                                    const ModuleCallbacks& h_module, ModuleScratch& scratch, CudaSlice<bf16>& z_h,
+                                    CudaSlice<bf16>& z_l) const {
+  const size_t rows = scratch.rows, hidden = config.hidden_size;
+  embedding_lookup(input_ids, embed_table, z_h, 1, rows, hidden, vocab_size, config.embedding_scale);
+  broadcast_vec(z_l, z_l_init, rows, hidden);
+  size_t slot = 0;
+  auto run = [&](const ModuleCallbacks& m, CudaSlice<bf16>& z_a, const CudaSlice<bf16>& z_b) {
+    LayerCallbacks cb;
+    const size_t base = slot;
+    cb.attention = [&m, base](size_t i, const CudaSlice<bf16>& n, CudaSlice<bf16>& out) {
+      m.attention(i, base + i, n, out);
+    };
+    cb.gate_up = m.gate_up;
+    cb.down = m.down;
+    transformer_module(z_a, z_b, z_a, m.n_layers, cb, scratch);
+    slot += m.n_layers;
+  };
+  for (size_t h = 0; h < h_cycles; ++h) {
+    for (size_t l = 0; l < l_cycles; ++l) run(l_module, z_l, z_h);
+    run(h_module, z_h, z_l);
+  }
+}
+
 }  // namespace hrm

@@ -177,6 +177,27 @@ class HrmLayerOps {
   void transformer_module(const CudaSlice<bf16>& z_a, const CudaSlice<bf16>& z_b, CudaSlice<bf16>& output,
                           size_t n_layers, const LayerCallbacks& layer, ModuleScratch& scratch) const;
 
+  // One module (H or L) of recurrent_forward; its attention is also given the
+  // KV-cache slot of the layer.
+  struct ModuleCallbacks {
+    size_t n_layers = 0;
+    std::function<void(size_t layer, size_t kv_slot, const CudaSlice<bf16>& normed, CudaSlice<bf16>& attn_out)>
+        attention;
+    std::function<void(size_t layer, const CudaSlice<bf16>& normed, CudaSlice<bf16>& gate, CudaSlice<bf16>& up)>
+        gate_up;
+    std::function<void(size_t layer, const CudaSlice<bf16>& act, CudaSlice<bf16>& down)> down;
+  };
+  // The HRM recurrent loop over scratch.rows tokens (src/lib.rs:1189-1270):
+  // z_h = embedding_lookup(input_ids) * config.embedding_scale (1189-1200),
+  // z_l = broadcast(z_l_init) (1202-1203), then for each of h_cycles:
+  // l_cycles x z_l = L(z_l + z_h), then z_h = H(z_h + z_l), each module pass
+  // through transformer_module.  KV-cache slots are numbered as the reference's
+  // kv_slot_counter: each module pass takes the next n_layers slots.
+  void recurrent_forward(const CudaSlice<uint32_t>& input_ids, const CudaSlice<bf16>& embed_table,
+                         size_t vocab_size, const CudaSlice<bf16>& z_l_init, size_t h_cycles, size_t l_cycles,
+                         const ModuleCallbacks& l_module, const ModuleCallbacks& h_module, ModuleScratch& scratch,
+                         CudaSlice<bf16>& z_h, CudaSlice<bf16>& z_l) const;
+
   // Builds the fp32 cos/sin table for config.head_dim / config.rope_theta
   // covering positions [0, max_positions); rope_embed uses it from then on
   // for every call it covers, and evaluates angles in-kernel otherwise.

@@ -358,6 +358,111 @@ void test_transformer_module(HrmLayerOps&) {
   expect(thrown, "output aliasing z_b rejected");
 }
 
+// recurrent_forward == the reference's loop (src/lib.rs:1189-1270) built from
+// the unfused wrappers and device copies: embedding, broadcast, then 2 H-cycles
+// x 3 L-cycles of 2-layer modules; the attention sees the reference's KV slots.
+void test_recurrent_forward(HrmLayerOps&) {
+  hrm::HrmConfig cfg;
+  cfg.hidden_size = 256;
+  cfg.intermediate_size = 512;
+  cfg.norm_eps = 1e-5f;
+  cfg.embedding_scale = 16.0f;
+  HrmLayerOps m(0, cfg);
+  const size_t rows = 40, H = 256, I = 512, L = 2, V = 50, n = rows * H;
+  cudaStream_t st = m.cu_stream();
+  auto copy2d = [&](bf16* dst, size_t dpitch, const bf16* src, size_t spitch, size_t width) {
+    expect(cudaMemcpy2DAsync(dst, dpitch * sizeof(bf16), src, spitch * sizeof(bf16), width * sizeof(bf16), rows,
+                             cudaMemcpyDeviceToDevice, st) == cudaSuccess,
+           "cudaMemcpy2DAsync");
+  };
+  auto copy = [&](CudaSlice<bf16>& dst, const CudaSlice<bf16>& src) {
+    expect(cudaMemcpyAsync(dst.device_ptr(), src.device_ptr(), n * sizeof(bf16), cudaMemcpyDeviceToDevice, st) ==
+               cudaSuccess,
+           "cudaMemcpyAsync");
+  };
+  std::vector<size_t> slots;
+  HrmLayerOps::ModuleCallbacks mod;
+  mod.n_layers = L;
+  mod.attention = [&](size_t, size_t slot, const CudaSlice<bf16>& nn, CudaSlice<bf16>& a) {
+    slots.push_back(slot);
+    copy2d(a.device_ptr(), H, nn.device_ptr(), H, H);
+  };
+  mod.gate_up = [&](size_t, const CudaSlice<bf16>& nn, CudaSlice<bf16>& g, CudaSlice<bf16>& u) {
+    for (CudaSlice<bf16>* t : {&g, &u}) {
+      copy2d(t->device_ptr(), I, nn.device_ptr(), H, H);
+      copy2d(t->device_ptr() + H, I, nn.device_ptr(), H, H);
+    }
+  };
+  mod.down = [&](size_t, const CudaSlice<bf16>& act, CudaSlice<bf16>& d) {
+    copy2d(d.device_ptr(), H, act.device_ptr(), I, H);
+  };
+
+  std::vector<uint32_t> ids(rows);
+  std::vector<float> table(V * H), init(H);
+  uint32_t state = 777u;
+  auto next = [&]() {
+    state = state * 1664525u + 1013904223u;
+    return ((state >> 8) * (1.0f / 16777216.0f)) * 2.0f - 1.0f;
+  };
+  for (size_t i = 0; i < rows; ++i) ids[i] = (uint32_t)((i * 7919u) % (V + 3));  // a few out of range
+  for (float& t : table) t = next() * 0.1f;
+  for (float& t : init) t = next();
+  auto d_ids = m.htod_copy_u32(ids);
+  auto d_table = m.htod_copy_bf16(to_bf16(table));
+  auto d_init = m.htod_copy_bf16(to_bf16(init));
+
+  // the fused loop
+  auto fh = m.alloc_zero_bf16(n), fl = m.alloc_zero_bf16(n);
+  HrmLayerOps::ModuleScratch scratch(m, rows);
+  m.recurrent_forward(d_ids, d_table, V, d_init, 2, 3, mod, mod, scratch, fh, fl);
+  const std::vector<size_t> fused_slots = slots;
+  slots.clear();
+
+  // the reference's order
+  auto rh = m.alloc_zero_bf16(n), rl = m.alloc_zero_bf16(n);
+  m.embedding_lookup(d_ids, d_table, rh, 1, rows, H, V, cfg.embedding_scale);
+  m.broadcast_vec(rl, d_init, rows, H);
+  auto tmp1 = m.alloc_zero_bf16(n), tmp2 = m.alloc_zero_bf16(n), norm_buf = m.alloc_zero_bf16(n);
+  auto attn_out = m.alloc_zero_bf16(n), norm2 = m.alloc_zero_bf16(n), down = m.alloc_zero_bf16(n);
+  auto res = m.alloc_zero_bf16(n), g = m.alloc_zero_bf16(rows * I), u = m.alloc_zero_bf16(rows * I);
+  auto act = m.alloc_zero_bf16(rows * I);
+  size_t slot = 0;
+  auto reference_module = [&](CudaSlice<bf16>& out, const CudaSlice<bf16>& z_b) {
+    m.additive_inject(out, z_b, tmp1, n);
+    copy(tmp2, tmp1);
+    for (size_t i = 0; i < L; ++i) {
+      CudaSlice<bf16>* x = &tmp2;
+      if (i > 0) {
+        copy(tmp1, out);
+        x = &tmp1;
+      }
+      m.rms_norm(*x, norm_buf, rows, H);
+      mod.attention(i, slot + i, norm_buf, attn_out);
+      m.additive_inject(*x, attn_out, out, n);
+      m.rms_norm(out, norm2, rows, H);
+      mod.gate_up(i, norm2, g, u);
+      m.swiglu_ffn(g, u, act, rows * I);
+      mod.down(i, act, down);
+      m.additive_inject(out, down, res, n);
+      copy(out, res);
+    }
+    m.rms_norm(out, tmp1, rows, H);
+    copy(out, tmp1);
+    slot += L;
+  };
+  for (int h = 0; h < 2; ++h) {
+    for (int l = 0; l < 3; ++l) reference_module(rl, rh);
+    reference_module(rh, rl);
+  }
+  expect(fused_slots == slots, "KV slot numbering");
+  expect(fused_slots.size() == 2 * 4 * L && fused_slots.back() == 2 * 4 * L - 1, "slots 0 .. 15 in order");
+  const auto want_h = m.sync_reclaim(std::move(rh)), want_l = m.sync_reclaim(std::move(rl));
+  const auto got_h = m.sync_reclaim(std::move(fh)), got_l = m.sync_reclaim(std::move(fl));
+  size_t bad = 0;
+  for (size_t i = 0; i < n; ++i) bad += (got_h[i].bits != want_h[i].bits) + (got_l[i].bits != want_l[i].bits);
+  expect(bad == 0, std::to_string(bad) + " elements of z_H / z_L differ from the reference's loop");
+}
+
 }  // namespace
 
 int main() {
@@ -371,6 +476,7 @@ int main() {
       {"test_pending_error_not_claimed", test_pending_error_not_claimed},
       {"test_raw_to_bf16", test_raw_to_bf16},
       {"test_transformer_module", test_transformer_module},
+      {"test_recurrent_forward", test_recurrent_forward},
   };
   try {
     HrmLayerOps hrm(0);

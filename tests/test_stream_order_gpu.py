@@ -99,3 +99,24 @@ def test_graph_replay_of_dependent_launches(oracle, cuda):
     torch.cuda.synchronize()
     assert_bits_equal(to_host(dx), _oracle_elementwise(oracle, x, u, b, 64), "x after 4 replays")
     del g
+
+
+def test_two_streams_concurrently(oracle, cuda):
+    """Two independent dependent-launch chains on two streams at once, joined
+    by events: each equals its own oracle sequence."""
+    rng = np.random.default_rng(15)
+    xs = [normal_bf16(rng, N, 0.5) for _ in range(2)]
+    u, b = normal_bf16(rng, N, 0.5), normal_bf16(rng, N, 0.05)
+    du, db = to_dev(u, cuda), to_dev(b, cuda)
+    streams = [torch.cuda.Stream(cuda) for _ in range(2)]
+    dxs = [to_dev(x, cuda) for x in xs]
+    dys = [torch.empty_like(dxs[0]) for _ in range(2)]
+    torch.cuda.synchronize()
+    for _ in range(100):
+        for i, s in enumerate(streams):
+            ops.swiglu_ffn(dxs[i], du, out=dys[i], stream=s)
+            ops.additive_inject(dys[i], db, out=dxs[i], stream=s)
+    for s in streams:
+        torch.cuda.current_stream(cuda).wait_stream(s)
+    for i in range(2):
+        assert_bits_equal(to_host(dxs[i]), _oracle_elementwise(oracle, xs[i], u, b, 100), f"stream {i}")
