@@ -32,9 +32,9 @@ __global__ void __launch_bounds__(kThreads) embedding_warp_kernel(const uint32_t
                                                                   uint4* out, int64_t tokens, int nchunks,
                                                                   uint32_t vocab, float scale) {
   grid_dependency_begin();
-  const int lane = threadIdx.x & 31;
-  const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
-  for (int64_t t = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); t < tokens; t += warp_stride) {
+  const int lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int64_t warp_stride = (int64_t)gridDim.x * nwarps;
+  for (int64_t t = (int64_t)blockIdx.x * nwarps + (threadIdx.x >> 5); t < tokens; t += warp_stride) {
     uint32_t id = ids[t];
     if (id >= vocab) id = vocab - 1;
     const uint4* src = table + (int64_t)id * nchunks;
@@ -86,10 +86,11 @@ cudaError_t launch_embedding(const uint32_t* ids, const void* table, void* out, 
   cudaError_t err = cudaSuccess;
   const int64_t wave = (int64_t)device_sm_count() * (2048 / kThreads);
   if (hidden % 8 == 0 && hidden / 8 <= INT32_MAX && aligned16(table) && aligned16(out)) {
-    int64_t blocks = (tokens + kWarps - 1) / kWarps;
+    const int nw = warps_per_cta(tokens, kWarps);
+    int64_t blocks = (tokens + nw - 1) / nw;
     if (HRM_EMB_WAVES > 0 && blocks > wave * HRM_EMB_WAVES) blocks = wave * HRM_EMB_WAVES;
     if (blocks > INT32_MAX) blocks = INT32_MAX;
-    err = launch_kernel(embedding_warp_kernel, blocks, kThreads, 0, s, ids, static_cast<const uint4*>(table),
+    err = launch_kernel(embedding_warp_kernel, blocks, 32 * nw, 0, s, ids, static_cast<const uint4*>(table),
         static_cast<uint4*>(out), tokens,
         (int)(hidden / 8), (uint32_t)vocab, scale);
   } else {

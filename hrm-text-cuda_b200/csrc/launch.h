@@ -13,6 +13,16 @@ int device_sm_count();
 // True when p is 16-byte aligned (a uint4 access is legal).
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Warps per CTA of a one-warp-per-row launch over `rows` rows: max_warps, or
+// fewer when there are fewer than max_warps rows per SM, so that a small
+// (decode-size) launch spreads over as many SMs as it has rows instead of
+// rows / max_warps of them.
+inline int warps_per_cta(int64_t rows, int max_warps) {
+  const int64_t per_sm = rows / device_sm_count();
+  if (per_sm >= max_warps) return max_warps;
+  return per_sm < 1 ? 1 : (int)per_sm;
+}
+
 // Programmatic dependent launches (1) or plain stream-ordered ones (0).
 #ifndef HRM_PDL
 #define HRM_PDL 1

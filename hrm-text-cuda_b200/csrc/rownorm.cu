@@ -181,7 +181,7 @@ __device__ __forceinline__ void accum8(float (&p)[8], const uint4& v) {
 // runs the first iteration of the row loop -- a warp without a row does no
 // memory work -- so that all threads reach that barrier.
 __device__ __forceinline__ void issue_weight(uint4* s_w, const uint4* w, int nchunks) {
-  for (int c = threadIdx.x; c < nchunks; c += kThreads) cp_async16(&s_w[c], w + c);
+  for (int c = threadIdx.x; c < nchunks; c += blockDim.x) cp_async16(&s_w[c], w + c);
   cp_async_commit();
 }
 __device__ __forceinline__ void publish_weight() {
@@ -204,8 +204,9 @@ __global__ void __launch_bounds__(kThreads, rownorm_min_blocks<VPL, MODE>()) row
   const int lane = threadIdx.x & 31;
   if (HAS_W) issue_weight(s_w, a.w, a.nchunks);
 
-  const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
-  int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int nwarps = blockDim.x >> 5;  // kWarps, or fewer for a small launch
+  const int64_t warp_stride = (int64_t)gridDim.x * nwarps;
+  int64_t row = (int64_t)blockIdx.x * nwarps + (threadIdx.x >> 5);
   for (bool first = true; first || row < a.rows; first = false, row += warp_stride) {
     const bool active = row < a.rows;  // uniform across the warp
     const uint4* src = a.x;
@@ -439,8 +440,9 @@ __global__ void __launch_bounds__(kThreads, HRM_RN_F32_MINBLOCKS) rms_f32_warp_k
   const int lane = threadIdx.x & 31;
   if (HAS_W) issue_weight(s_w4, reinterpret_cast<const uint4*>(a.w), a.nchunks);
 
-  const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
-  int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int nwarps = blockDim.x >> 5;  // kWarps, or fewer for a small launch
+  const int64_t warp_stride = (int64_t)gridDim.x * nwarps;
+  int64_t row = (int64_t)blockIdx.x * nwarps + (threadIdx.x >> 5);
   for (bool first = true; first || row < a.rows; first = false, row += warp_stride) {
     const bool active = row < a.rows;  // uniform across the warp
     const int64_t base = row * a.nchunks;
@@ -591,11 +593,12 @@ cudaError_t launch_warp_on(const RowArgs& a, cudaStream_t s) {
     occ.store(o, std::memory_order_relaxed);
   }
   const size_t smem = HAS_W ? (size_t)a.nchunks * 16 : 0;
-  int64_t blocks = (a.rows + kWarps - 1) / kWarps;
+  const int nw = warps_per_cta(a.rows, kWarps);
+  int64_t blocks = (a.rows + nw - 1) / nw;
   const int64_t wave = (int64_t)device_sm_count() * o;
   if (HRM_RN_WAVES > 0 && blocks > wave * HRM_RN_WAVES) blocks = wave * HRM_RN_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;
-  err = launch_kernel(kernel, blocks, kThreads, smem, s, a);
+  err = launch_kernel(kernel, blocks, 32 * nw, smem, s, a);
   return err;
 }
 
@@ -746,11 +749,12 @@ cudaError_t launch_f32_warp(const RowArgsF32& a, cudaStream_t s) {
     occ.store(o, std::memory_order_relaxed);
   }
   const size_t smem = HAS_W ? (size_t)a.nchunks * 16 : 0;
-  int64_t blocks = (a.rows + kWarps - 1) / kWarps;
+  const int nw = warps_per_cta(a.rows, kWarps);
+  int64_t blocks = (a.rows + nw - 1) / nw;
   const int64_t wave = (int64_t)device_sm_count() * o;
   if (HRM_RN_F32_WAVES > 0 && blocks > wave * HRM_RN_F32_WAVES) blocks = wave * HRM_RN_F32_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;
-  err = launch_kernel(kernel, blocks, kThreads, smem, s, a);
+  err = launch_kernel(kernel, blocks, 32 * nw, smem, s, a);
   return err;
 }
 

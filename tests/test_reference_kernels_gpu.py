@@ -227,7 +227,7 @@ def test_throughput_vs_reference_kernels(ref, cuda):
     nb = 65536 * (4 + 2 * 2 * 2048)
     res["embedding"] = (nb / _time(lambda: ops.embedding_lookup(ids, tab, 45.254834, out=eo)),
                         nb / _time(lambda: ref.embedding_lookup(ids, tab, eo, 45.254834)))
-    del tab, eo
+    del eo
     # one 4-layer module pass over 16384 tokens (H 2048, I 5632), attention and
     # GEMM outputs pre-filled (the stand-ins do nothing): the fused schedule vs
     # the reference's kernels in the reference's order with its device copies.
@@ -267,13 +267,35 @@ def test_throughput_vs_reference_kernels(ref, cuda):
     del sc, bufs
     out = {k: {"ours_gbs": round(a / 1e6, 1), "reference_gbs": round(b_ / 1e6, 1), "speedup": round(a / b_, 2)}
            for k, (a, b_) in res.items()}
+    # decode shapes: latency per call (us), 8 calls per CUDA graph
+    dq, dk = rn((8, 16, 1, 128)), rn((8, 16, 1, 128))
+    ids64 = ids[:64].contiguous()
+    e64 = torch.empty((64, 2048), dtype=bf, device=cuda)
+    x64, b64 = rn((64, 2048)), rn((64, 2048))
+    r64, y64 = torch.empty_like(x64), torch.empty_like(x64)
+    g64, u64 = rn((64, 5632), 0.5), rn((64, 5632), 0.5)
+    o64 = torch.empty_like(g64)
+    tab4096 = ops.rope_table(4096, 128)
+    dec = {
+        "rope_decode_8x16x1x128_off4095": (lambda: ops.rope_embed(dq, dk, 4095, 10000.0, tab4096),
+                                           lambda: ref.rope_embed(dq, dk, 4095, 10000.0)),
+        "embedding_decode_64_ids": (lambda: ops.embedding_lookup(ids64, tab, 45.254834, out=e64),
+                                    lambda: ref.embedding_lookup(ids64, tab, e64, 45.254834)),
+        "add_rms_norm_decode_64x2048": (lambda: ops.add_rms_norm(x64, b64, None, 1e-5, residual_out=r64,
+                                                                  normed_out=y64),
+                                        lambda: (ref.additive_inject(x64, b64, r64), ref.rms_norm(r64, y64, 1e-5))),
+        "swiglu_decode_64x5632": (lambda: ops.swiglu_ffn(g64, u64, out=o64), lambda: ref.swiglu_ffn(g64, u64, o64)),
+    }
+    for k, (ours, theirs) in dec.items():
+        a_us, b_us = _time_graph([ours] * 8) * 1e3, _time_graph([theirs] * 8) * 1e3
+        out[k] = {"ours_us": round(a_us, 2), "reference_us": round(b_us, 2), "speedup": round(b_us / a_us, 2)}
     print(json.dumps({"vs_reference_kernels": out}))
     path = os.environ.get("HRM_REF_TIMING_OUT")
     if path:
         with open(path, "w") as f:
             json.dump(out, f, indent=1)
     for k, v in out.items():
-        assert v["speedup"] >= 0.95, (k, v)
+        assert v["speedup"] >= (0.8 if "decode" in k else 0.95), (k, v)
 
 
 @pytest.mark.parametrize("b,s,h,d,off", [(2, 256, 16, 128, 0), (8, 1, 16, 128, 4095), (1, 77, 12, 64, 3)])
