@@ -12,10 +12,15 @@ heads x 128; --qk-layout head for the reference's [B, 16, S, 128]) with a fp32
 cos/sin table,
 residual add + RMSNorm [65536 x 2048], SwiGLU [65536 x 5632] ~ 0.5 N(0, 1);
 norm weights 1 + 0.1 N(0, 1), eps 1e-5, scale sqrt(2048), theta 1e4.  Inputs
-are synthetic (seeded), generated on the device.  A step is one pass over
-the rank's 65536 tokens; rows (tokens) are independent, so N GPUs run N
-disjoint shards of an N x 65536-token job with no collective on the data
-path (weak scaling).
+are synthetic, generated on the device by a counter-based generator keyed by
+(seed, tensor, global index), so rank r holds global tokens [r T, (r + 1) T)
+of one job-wide tensor set.  A step is one pass over the rank's 65536
+tokens; rows (tokens) are independent, so N GPUs run N disjoint shards of an
+N x 65536-token job with no collective on the data path (weak scaling).
+
+The other workloads are the single layer-op configurations (their K timed
+steps replayed from a CUDA graph) and `module`, one 4-layer pass of the
+layer loop's residual / norm / SwiGLU schedule.
 
 The metric is algorithmic HBM GB/s: the bytes the pass must move per token
 (70,660 B: ids, gathered rows, n1, Q/K read+write, o, r, n2, gate/up, y --
@@ -27,8 +32,9 @@ One JSON line on rank 0 carries: value (device-resident, CUDA events, max
 over ranks), e2e (pinned host buffers -> device -> host through the public
 API, copies overlapped with the kernels), the roofline of the dominant
 kernel (SwiGLU), per-kernel times, the 64-token decode-shape latency (CUDA
-graph), the clocks sampled during the timed region and the oracle's
-multithreaded CPU throughput on a bounded sample.
+graph, median of 5), the clocks sampled during the timed region and the
+oracle's multithreaded CPU throughput on a bounded sample.  Under torchrun,
+every rank checks its peers' heartbeats before each collective.
 
 --impl reference times the reference's path on the CPU (the oracle: a C
 restatement of the reference kernels, all host threads) on the same metric.
