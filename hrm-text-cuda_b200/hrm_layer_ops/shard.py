@@ -115,9 +115,17 @@ class PeerMonitor:
 
     @classmethod
     def for_default_group(cls, prefix: str = "hrm/peer") -> "PeerMonitor":
+        """A monitor on the default process group's own key-value store (the one
+        its rendezvous created), so no extra port or server is needed.  torch
+        exposes that store only through distributed_c10d._get_default_store;
+        pass a store to the constructor where that helper is missing."""
         from torch.distributed import distributed_c10d as c10d
 
-        return cls(c10d._get_default_store(), dist.get_rank(), dist.get_world_size(), prefix)
+        get = getattr(c10d, "_get_default_store", None)
+        if get is None:
+            raise RuntimeError("this torch has no distributed_c10d._get_default_store: "
+                               "construct PeerMonitor(store, rank, world) with a store of your own")
+        return cls(get(), dist.get_rank(), dist.get_world_size(), prefix)
 
     def _hb(self, r: int) -> str:
         return f"{self.prefix}/hb/{r}"
