@@ -1,0 +1,50 @@
+"""CPU: the benchmark's reference arm and its JSON line (no GPU needed).
+
+`bench.py --impl reference` times the reference's path restated on the host
+(the oracle) and prints exactly one JSON line with the metric, the CPU
+baseline and an e2e object; a workload it does not cover prints an
+`unavailable` line and exits 0.
+"""
+
+import json
+import os
+import subprocess
+import sys
+
+from conftest import ROOT
+
+
+def run_bench(*args, timeout=600):
+    env = dict(os.environ, OMP_NUM_THREADS="4")
+    res = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], capture_output=True, text=True,
+                         timeout=timeout, env=env, cwd=ROOT)
+    lines = [l for l in res.stdout.splitlines() if l.startswith("{")]
+    return res, lines
+
+
+def test_reference_arm_prints_one_contract_line():
+    res, lines = run_bench("--impl", "reference", "--steps", "1", "--warmup", "3")
+    assert res.returncode == 0, res.stderr[-2000:]
+    assert len(lines) == 1, res.stdout[-2000:]
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["unit"] == "GB/s" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["steps"] == 1 and d["warmup"] == 3
+    assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+
+
+def test_reference_arm_other_workload_is_unavailable():
+    res, lines = run_bench("--impl", "reference", "--workload", "swiglu", "--steps", "1", "--warmup", "3")
+    assert res.returncode == 0, res.stderr[-2000:]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unavailable"]
+
+
+def test_warmup_below_three_is_refused():
+    res, _ = run_bench("--warmup", "2", "--steps", "1", timeout=300)
+    assert res.returncode != 0 and "warmup" in (res.stderr + res.stdout)
