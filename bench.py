@@ -63,6 +63,14 @@ EPS, THETA = 1e-5, 10000.0
 SEED = 0                                  # seed of the counter-based chain inputs
 SCALE = 45.254833995939045                # (float)sqrt(2048)
 
+# --dims: the benchmark's 1B-class shapes (the default), or the reference's own
+# default model (HrmConfig, src/lib.rs:40-60: hidden 1536, 12 heads of 128,
+# intermediate 4096, vocab 65536, embedding scale sqrt(1536)).
+DIMS = {
+    "bench": dict(HIDDEN=2048, HEADS=16, HEAD_DIM=128, INTER=5632, VOCAB=32000, SCALE=45.254833995939045),
+    "hrm-text-1b": dict(HIDDEN=1536, HEADS=12, HEAD_DIM=128, INTER=4096, VOCAB=65536, SCALE=39.191835884530846),
+}
+
 
 def parse_args():
     ap = argparse.ArgumentParser()
@@ -80,7 +88,13 @@ def parse_args():
     ap.add_argument("--chunk-tokens", type=int, default=4096, help="e2e pipeline chunk (token-major Q/K)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-oracle baseline leg")
-    return ap.parse_args()
+    ap.add_argument("--dims", choices=sorted(DIMS), default="bench",
+                    help="chain / module shapes: the benchmark's (default) or the reference's default model")
+    args = ap.parse_args()
+    if args.dims != "bench" and args.workload not in ("chain", "module"):
+        ap.error("--dims applies to the chain and module workloads")
+    globals().update(DIMS[args.dims])
+    return args
 
 
 def load_peaks():
@@ -224,6 +238,7 @@ class Chain:
         self.kernel_bytes = {k: per[k] * T for k in self.kernels}
         self.footprint = per["op_sum"] * T
         self.config = {"workload": "chain: embed+RMSNorm -> RoPE -> add+RMSNorm -> SwiGLU",
+                       "dims": "hrm-text-1b" if HIDDEN == 1536 else "bench",
                        "tokens_per_gpu": T, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM,
                        "intermediate": INTER, "vocab": VOCAB, "qk_shape": list(qk),
                        "qk_layout": "token-major [B, S, heads, head_dim]" if token_major

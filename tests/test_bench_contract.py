@@ -48,3 +48,15 @@ def test_reference_arm_other_workload_is_unavailable():
 def test_warmup_below_three_is_refused():
     res, _ = run_bench("--warmup", "2", "--steps", "1", timeout=300)
     assert res.returncode != 0 and "warmup" in (res.stderr + res.stdout)
+
+
+def test_reference_arm_at_the_reference_model_dims():
+    res, lines = run_bench("--impl", "reference", "--dims", "hrm-text-1b", "--steps", "1", "--warmup", "3")
+    assert res.returncode == 0, res.stderr[-2000:]
+    d = json.loads(lines[0])
+    assert d["config"]["hidden"] == 1536 and d["config"]["intermediate"] == 4096
+
+
+def test_dims_only_for_chain_and_module():
+    res, _ = run_bench("--dims", "hrm-text-1b", "--workload", "swiglu", timeout=300)
+    assert res.returncode != 0 and "--dims" in res.stderr
