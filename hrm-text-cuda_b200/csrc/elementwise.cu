@@ -86,23 +86,25 @@ __device__ __forceinline__ uint4 apply8(const Op& op, const uint4& a, const uint
 }
 
 // a, b, out: 16-byte aligned; nvec = n / 8 full vectors; the n % 8 trailing
-// elements (starting at element nvec * 8) are done by global thread 0.
-template <class Op>
+// elements (starting at element nvec * 8) are done by global thread 0.  U
+// vectors per operand per thread: kUnroll, or 1 for a launch too small to
+// give every SM a CTA otherwise (decode sizes).
+template <class Op, int U>
 __global__ void __launch_bounds__(kThreads, HRM_EW_MINBLOCKS) ew_vec_kernel(const uint4* a, const uint4* b, uint4* out,
                                                           int64_t nvec, int tail) {
   grid_dependency_begin();
   const Op op;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-  for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
-    uint4 va[kUnroll], vb[kUnroll];
+  for (; i + (U - 1) * stride < nvec; i += U * stride) {
+    uint4 va[U], vb[U];
 #pragma unroll
-    for (int j = 0; j < kUnroll; ++j) {
+    for (int j = 0; j < U; ++j) {
       va[j] = ld_stream(a + i + j * stride);
       vb[j] = ld_stream(b + i + j * stride);
     }
 #pragma unroll
-    for (int j = 0; j < kUnroll; ++j) st_stream(out + i + j * stride, apply8(op, va[j], vb[j]));
+    for (int j = 0; j < U; ++j) st_stream(out + i + j * stride, apply8(op, va[j], vb[j]));
   }
   for (; i < nvec; i += stride) st_stream(out + i, apply8(op, ld_stream(a + i), ld_stream(b + i)));
 
@@ -132,10 +134,15 @@ cudaError_t launch_ew(const void* a, const void* b, void* out, int64_t n, cudaSt
   if (aligned16(a) && aligned16(b) && aligned16(out)) {
     const int64_t nvec = n / 8;
     int64_t blocks = (nvec + (int64_t)kThreads * kUnroll - 1) / ((int64_t)kThreads * kUnroll);
-    if (blocks < 1) blocks = 1;
+    if (blocks < device_sm_count()) {  // small launch: one vector per thread, more CTAs
+      blocks = (nvec + kThreads - 1) / kThreads;
+      if (blocks < 1) blocks = 1;
+      return launch_kernel(ew_vec_kernel<Op, 1>, blocks, kThreads, 0, s, static_cast<const uint4*>(a),
+          static_cast<const uint4*>(b), static_cast<uint4*>(out), nvec, (int)(n % 8));
+    }
     if (HRM_EW_WAVES > 0 && blocks > max_blocks * HRM_EW_WAVES) blocks = max_blocks * HRM_EW_WAVES;
     if (blocks > INT32_MAX) blocks = INT32_MAX;
-    err = launch_kernel(ew_vec_kernel<Op>, blocks, kThreads, 0, s, static_cast<const uint4*>(a),
+    err = launch_kernel(ew_vec_kernel<Op, kUnroll>, blocks, kThreads, 0, s, static_cast<const uint4*>(a),
         static_cast<const uint4*>(b), static_cast<uint4*>(out), nvec, (int)(n % 8));
   } else {
     int64_t blocks = (n + kThreads - 1) / kThreads;
