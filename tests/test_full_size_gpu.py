@@ -130,3 +130,44 @@ def test_chain_65536_tokens_and_decode(oracle, cuda):
         assert ulp_error(to_host(out[sel]), oracle.swiglu_ffn(g, u)).max() <= ULP_TOL
     torch.cuda.synchronize()
     assert ops.wait_timeouts() == 0  # no bounded device wait ran out
+
+
+def test_chain_at_the_reference_model_shapes(oracle, cuda):
+    """The chained pass at the reference's default model shapes (hidden 1536,
+    12 heads of 128, intermediate 4096, vocab 65536, scale sqrt(1536)) over
+    16384 tokens, token-major Q/K [4, 4096, 12, 128]: every output against the
+    oracle (SwiGLU on 2048 sampled rows)."""
+    from hrm_layer_ops import chain
+
+    rng = np.random.default_rng(6)
+    H, HEADS, I, V, T, S = 1536, 12, 4096, 65536, 16384, 4096
+    scale, eps = float(np.float32(np.sqrt(1536.0))), 1e-5
+    table = normal_bf16(rng, (V, H), 0.02)
+    w1, w2 = normal_bf16(rng, H, 0.1, 1.0), normal_bf16(rng, H, 0.1, 1.0)
+    ids = rng.integers(0, V, T, dtype=np.uint32)
+    q, k = normal_bf16(rng, (T // S, S, HEADS, 128)), normal_bf16(rng, (T // S, S, HEADS, 128))
+    o = normal_bf16(rng, (T, H))
+    gen = torch.Generator(device=cuda).manual_seed(6)
+    dg = (torch.randn((T, I), generator=gen, device=cuda) * 0.5).to(torch.bfloat16)
+    du = (torch.randn((T, I), generator=gen, device=cuda) * 0.5).to(torch.bfloat16)
+    w = chain.ChainWeights(table=to_dev(table, cuda), w1=to_dev(w1, cuda), w2=to_dev(w2, cuda),
+                           rope=ops.rope_table(S, 128), scale=scale, eps=eps, theta=10000.0)
+    dq, dk = to_dev(q, cuda), to_dev(k, cuda)
+    bf = dict(dtype=torch.bfloat16, device=cuda)
+    h, n1, r, n2 = (torch.empty((T, H), **bf) for _ in range(4))
+    y = torch.empty((T, I), **bf)
+    chain.run_device(w, to_dev(ids, cuda), dq, dk, to_dev(o, cuda), dg, du, h, n1, r, n2, y, 0, token_major=True)
+    wh, wn1 = oracle.embed_rms_norm(ids, table, scale, w1, eps)
+    wr, wn2 = oracle.add_rms_norm(wh, o, w2, eps)
+    assert_bits_equal(to_host(h), wh, "hidden")
+    assert_bits_equal(to_host(n1), wn1, "norm1")
+    assert_bits_equal(to_host(r), wr, "residual")
+    assert_bits_equal(to_host(n2), wn2, "norm2")
+    hq, hk = q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3)  # the oracle's [B, H, S, D]
+    wq, wk = oracle.rope_embed(np.ascontiguousarray(hq), np.ascontiguousarray(hk), 0, 10000.0,
+                               oracle.rope_table(S, 128, 10000.0))
+    for got, want in ((to_host(dq).transpose(0, 2, 1, 3), wq), (to_host(dk).transpose(0, 2, 1, 3), wk)):
+        assert ulp_error(np.ascontiguousarray(got), want, rope_pair_magnitude(want)).max() <= ULP_TOL
+    rows = np.sort(rng.choice(T, 2048, replace=False))
+    sel = torch.from_numpy(rows).to(cuda)
+    assert ulp_error(to_host(y[sel]), oracle.swiglu_ffn(to_host(dg[sel]), to_host(du[sel]))).max() <= ULP_TOL
