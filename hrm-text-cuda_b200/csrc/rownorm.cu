@@ -6,10 +6,12 @@
 // registers, so the row is read from HBM exactly once (the reference reads it
 // twice, src/kernels/rms_norm.cu:28 and :62).  Lane l holds the 16-byte chunks
 // l, l+32, l+64, ... of its row, so every warp-wide access is one contiguous
-// 512-byte span.  A CTA of 8 warps stages the optional weight vector into
-// shared memory once with cp.async; the grid has one warp per row (measured on
-// B200: 6.7 TB/s for add + RMSNorm vs 6.05 TB/s with a persistent one-wave
-// grid), and the warps still loop if a launch exceeds the grid limit.
+// 512-byte span.  A CTA of 8 warps (fewer for a launch with fewer than 8 rows
+// per SM, so that small launches spread over more SMs) copies the optional
+// weight vector into shared memory with cp.async while its first rows load;
+// the grid has one warp per row (measured on B200: 6.7 TB/s for add + RMSNorm
+// vs 6.05 TB/s with a persistent one-wave grid), and the warps still loop if a
+// launch exceeds the grid limit.
 //
 // Reduction order.  rms_norm_kernel runs 256 threads per row: thread t
 // accumulates x[t], x[t+256], ... with fused multiply-add (src/kernels/
