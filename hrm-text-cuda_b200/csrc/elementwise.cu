@@ -13,7 +13,9 @@
 //     for SwiGLU, against 6.50 with 4 resident CTAs and 6.06 for a persistent
 //     one-wave grid with 4 vectors in flight per thread.  (Pairing the fp32
 //     multiplies into f32x2 instructions measured slower at every occupancy.)
-//   * evict-first loads/stores so the stream does not flush reused L2 lines.
+//   * evict-first loads/stores so the stream does not flush reused L2 lines;
+//   * a launch too small to give every SM a CTA that way (decode sizes) takes
+//     one vector per thread instead, doubling its CTAs.
 // The arithmetic per element is the reference's, operation for operation:
 //   swiglu: g * (1.0f / (1.0f + __expf(-g))) * u    (src/kernels/swiglu_ffn.cu:31-35)
 //   add   : a + b                                   (src/kernels/additive_inject.cu:29-31)

@@ -6,6 +6,8 @@
 // lane, lane+32, ... with up to 8 loads in flight before the first store.
 // Table rows are loaded with normal caching (ids repeat, and a 2048-wide bf16
 // row is 4 KB of reusable L2 data); the output is streamed (evict-first).
+// CTAs have 8 warps, or fewer when there are fewer than 8 tokens per SM, so a
+// decode-size gather (64 ids) runs on 64 SMs.
 // Arithmetic per element: one fp32 multiply and one RNE rounding, exactly
 // src/kernels/embedding_lookup.cu:44-47, so the result is bit-exact.
 #include "common.cuh"
