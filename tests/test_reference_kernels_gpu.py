@@ -333,3 +333,22 @@ def test_attn_gate_and_broadcast_match_reference(ref, rng, cuda):
     rb = torch.empty((1000, 1536), dtype=torch.bfloat16, device=cuda)
     ref.broadcast_vec(rb, src)
     assert_bits_equal(to_host(ops.broadcast_vec(src, 1000)), to_host(rb), "broadcast_vec")
+
+
+@pytest.mark.parametrize("theta,off,s", [(500000.0, 30000, 64), (1000000.0, 8191, 1), (10000.0, 65535, 3)])
+@pytest.mark.parametrize("use_table", [False, True])
+def test_rope_long_context_matches_reference(ref, oracle, rng, cuda, theta, off, s, use_table):
+    """Large theta and positions far beyond 4096 (fp32 angles up to ~6.5e4 rad):
+    bit-identical to the reference kernel, <= 2 bf16 ulp (at pair magnitude)
+    of the oracle."""
+    b, h, d = 2, 8, 128
+    q, k = normal_bf16(rng, (b, h, s, d)), normal_bf16(rng, (b, h, s, d))
+    rq, rk = to_dev(q, cuda), to_dev(k, cuda)
+    ref.rope_embed(rq, rk, off, theta)
+    mq, mk = to_dev(q, cuda), to_dev(k, cuda)
+    ops.rope_embed(mq, mk, off, theta, ops.rope_table(off + s, d, theta) if use_table else None)
+    assert_bits_equal(to_host(mq), to_host(rq), "q vs reference")
+    assert_bits_equal(to_host(mk), to_host(rk), "k vs reference")
+    oq, ok = oracle.rope_embed(q, k, off, theta)
+    for got, want in ((to_host(mq), oq), (to_host(mk), ok)):
+        assert ulp_error(got, want, rope_pair_magnitude(want)).max() <= ULP_TOL
