@@ -352,3 +352,42 @@ def test_rope_long_context_matches_reference(ref, oracle, rng, cuda, theta, off,
     oq, ok = oracle.rope_embed(q, k, off, theta)
     for got, want in ((to_host(mq), oq), (to_host(mk), ok)):
         assert ulp_error(got, want, rope_pair_magnitude(want)).max() <= ULP_TOL
+
+
+def _special_rows(rng, rows, hidden):
+    """Rows mixing NaN, +-inf, zeros, denormals and values near the bf16 limit
+    into normal data; some rows stay all-normal."""
+    x = normal_bf16(rng, (rows, hidden))
+    specials = np.array([0x7FC0, 0xFFC0, 0x7F80, 0xFF80, 0x0000, 0x8000, 0x0001, 0x807F, 0x7F7F, 0xFF7F],
+                        np.uint16)
+    for r in range(0, rows, 2):
+        cols = rng.choice(hidden, 3, replace=False)
+        x[r, cols] = rng.choice(specials, 3)
+    return x
+
+
+def test_special_values_match_reference(ref, rng, cuda):
+    """NaN, inf, denormal and near-overflow inputs through add, add + RMSNorm,
+    RMSNorm, SwiGLU and the embedding gather (with an overflowing scale): the
+    same bits as the reference kernels."""
+    rows, hidden = 64, 2048
+    x, b = _special_rows(rng, rows, hidden), _special_rows(rng, rows, hidden)
+    dx, db = to_dev(x, cuda), to_dev(b, cuda)
+    r_ref, y_ref = torch.empty_like(dx), torch.empty_like(dx)
+    ref.additive_inject(dx, db, r_ref)
+    ref.rms_norm(r_ref, y_ref, 1e-5)
+    r, y = ops.add_rms_norm(dx, db, None, 1e-5)
+    assert_bits_equal(to_host(r), to_host(r_ref), "residual")
+    assert_bits_equal(to_host(y), to_host(y_ref), "normed")
+    ref.rms_norm(dx, y_ref, 1e-5)
+    assert_bits_equal(to_host(ops.rms_norm(dx, None, 1e-5)), to_host(y_ref), "rms_norm")
+    o_ref = torch.empty_like(dx)
+    ref.swiglu_ffn(dx, db, o_ref)
+    assert_bits_equal(to_host(ops.swiglu_ffn(dx, db)), to_host(o_ref), "swiglu")
+    table = _special_rows(rng, 100, hidden)
+    ids = rng.integers(0, 110, 300, dtype=np.uint32)
+    dt, di = to_dev(table, cuda), to_dev(ids, cuda)
+    e_ref = torch.empty((300, hidden), dtype=torch.bfloat16, device=cuda)
+    for scale in (1.0, 3.0e38, 1.0e-30):
+        ref.embedding_lookup(di, dt, e_ref, scale)
+        assert_bits_equal(to_host(ops.embedding_lookup(di, dt, scale)), to_host(e_ref), f"embedding x {scale}")
