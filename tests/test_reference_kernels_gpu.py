@@ -319,6 +319,25 @@ def test_split_gqkv_rope_matches_reference_sequence(ref, rng, cuda, b, s, h, d, 
         assert_bits_equal(to_host(got), to_host(want), name)
 
 
+@pytest.mark.parametrize("b,s,h,d", [(2, 256, 16, 128), (1, 77, 12, 64), (3, 5, 2, 128)])
+def test_split_gqkv_rope_matches_reference_prefill_cache_form(ref, rng, cuda, b, s, h, d):
+    """The prefill form of the reference's cache write (kv_cache_update with
+    is_decode false, cached_len 0) == the fused op with cache_offset 0."""
+    gqkv = to_dev(normal_bf16(rng, (b, s, 4 * h * d)), cuda)
+    cache_len = s + 3
+    kc0, vc0 = to_dev(normal_bf16(rng, (b, h, cache_len, d)), cuda), to_dev(normal_bf16(rng, (b, h, cache_len, d)), cuda)
+    rg = torch.empty((b, s, h, d), dtype=torch.bfloat16, device=cuda)
+    rq, rk, rv = (torch.empty((b, h, s, d), dtype=torch.bfloat16, device=cuda) for _ in range(3))
+    rkc, rvc = kc0.clone(), vc0.clone()
+    ref.split_gqkv(gqkv, rg, rq, rk, rv)
+    ref.rope_embed(rq, rk, 0, 10000.0)
+    ref.kv_cache_update(rk, rv, rkc, rvc, 0, False)
+    mkc, mvc = kc0.clone(), vc0.clone()
+    outs = ops.split_gqkv_rope(gqkv, h, 0, 10000.0, None, mkc, mvc, cache_offset=0)
+    for got, want, name in zip((*outs, mkc, mvc), (rg, rq, rk, rv, rkc, rvc), ("gate", "q", "k", "v", "kc", "vc")):
+        assert_bits_equal(to_host(got), to_host(want), name)
+
+
 def test_attn_gate_and_broadcast_match_reference(ref, rng, cuda):
     g, a = to_dev(normal_bf16(rng, 300007, 2.0), cuda), to_dev(normal_bf16(rng, 300007), cuda)
     g[:4] = torch.tensor([0.0, float("inf"), float("-inf"), float("nan")], dtype=torch.bfloat16)
