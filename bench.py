@@ -97,6 +97,49 @@ def parse_args():
     return args
 
 
+def chain_bytes_per_token(hidden, heads, head_dim, inter):
+    """Bytes each chain kernel must move per token (the gathered table row, not
+    the table; weights and the rope table are L2-resident constants).
+    'minimal' is the whole pass with every intermediate kept on chip: ids + row
+    + n1 + Q/K read and written + o + r + n2 + gate/up + y.  The library's
+    hrm_layer_ops.chain.algorithmic_bytes_per_token states the same counts
+    (a CPU test keeps the two equal); it is restated here so that the
+    reference arm imports nothing of the library."""
+    row, qk = 2 * hidden, 2 * heads * head_dim
+    per = {
+        "embed_rms_norm": 4 + row + row + row,   # id, table row, h, n1
+        "rope_embed": 2 * qk + 2 * qk,           # Q, K read and written
+        "add_rms_norm": 4 * row,                 # h, o read; r, n2 written
+        "swiglu_ffn": 3 * 2 * inter,             # gate, up read; y written
+    }
+    per["op_sum"] = sum(per[k] for k in CHAIN_KERNEL_NAMES)
+    per["minimal"] = 4 + row + row + 4 * qk + row + row + row + 2 * 2 * inter + 2 * inter
+    return per
+
+
+CHAIN_KERNEL_NAMES = ("embed_rms_norm", "rope_embed", "add_rms_norm", "swiglu_ffn")
+
+
+def chain_qk_shape(tokens, token_major):
+    batch = tokens // CHAIN_S
+    return (batch, CHAIN_S, HEADS, HEAD_DIM) if token_major else (batch, HEADS, CHAIN_S, HEAD_DIM)
+
+
+def chain_config(tokens, token_major, world):
+    """The chain workload's `config`, the same dict on both arms."""
+    per = chain_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)
+    return {"workload": "chain: embed+RMSNorm -> RoPE -> add+RMSNorm -> SwiGLU",
+            "dims": "hrm-text-1b" if HIDDEN == 1536 else "bench",
+            "tokens_per_gpu": tokens, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM,
+            "intermediate": INTER, "vocab": VOCAB, "qk_shape": list(chain_qk_shape(tokens, token_major)),
+            "qk_layout": "token-major [B, S, heads, head_dim]" if token_major
+            else "head-major [B, heads, S, head_dim]",
+            "bytes_per_token_minimal": per["minimal"], "bytes_per_token_moved": per["op_sum"],
+            "l2": f"inputs larger than L2 ({per['op_sum'] * tokens / 1e9:.1f} GB moved per step vs 126 MB L2); "
+                  "no flush",
+            "parallelism": f"{world} row shards, no collective"}
+
+
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -193,7 +236,7 @@ class Chain:
     data = ("synthetic, counter-based (splitmix64 + Box-Muller keyed by seed, tensor and global index), "
             "generated on the device; rank r holds global tokens [r*T, (r+1)*T)")
 
-    def __init__(self, device, rank, tokens=CHAIN_B * CHAIN_S, token_major=True, chunk_tokens=4096):
+    def __init__(self, device, rank, world, tokens=CHAIN_B * CHAIN_S, token_major=True, chunk_tokens=4096):
         import torch
 
         from hrm_layer_ops import chain, ops
@@ -220,7 +263,7 @@ class Chain:
             w2=nb("norm2_weight", (HIDDEN,), std=0.1, mean=1.0), rope=ops.rope_table(CHAIN_S, HEAD_DIM, THETA, device),
             scale=SCALE, eps=EPS, theta=THETA)
         self.ids = synth.ids(T, SEED, synth.tag_of("ids"), VOCAB, t0, device)
-        qk = (self.batch, CHAIN_S, HEADS, HEAD_DIM) if token_major else (self.batch, HEADS, CHAIN_S, HEAD_DIM)
+        qk = chain_qk_shape(T, token_major)
         self.q = nb("q", qk, t0 * HEADS * HEAD_DIM)
         self.k = nb("k", qk, t0 * HEADS * HEAD_DIM)
         self.o = nb("attn_out", (T, HIDDEN), t0 * HIDDEN)
@@ -230,21 +273,14 @@ class Chain:
         bf = dict(dtype=torch.bfloat16, device=device)
         self.h, self.n1, self.r, self.n2 = (e((T, HIDDEN), **bf) for _ in range(4))
         self.y = e((T, INTER), **bf)
-        per = chain.algorithmic_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)
+        per = chain_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)
         self.per_token = per
         self.bytes_per_step = per["minimal"] * T
         self.rows_per_step = T
-        self.kernels = list(chain.CHAIN_KERNELS)
+        self.kernels = list(CHAIN_KERNEL_NAMES)
         self.kernel_bytes = {k: per[k] * T for k in self.kernels}
         self.footprint = per["op_sum"] * T
-        self.config = {"workload": "chain: embed+RMSNorm -> RoPE -> add+RMSNorm -> SwiGLU",
-                       "dims": "hrm-text-1b" if HIDDEN == 1536 else "bench",
-                       "tokens_per_gpu": T, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM,
-                       "intermediate": INTER, "vocab": VOCAB, "qk_shape": list(qk),
-                       "qk_layout": "token-major [B, S, heads, head_dim]" if token_major
-                       else "head-major [B, heads, S, head_dim]",
-                       "bytes_per_token_minimal": per["minimal"], "bytes_per_token_moved": per["op_sum"],
-                       "l2": f"inputs larger than L2 ({per['op_sum'] * T / 1e9:.1f} GB moved per step vs 126 MB L2); no flush"}
+        self.config = chain_config(T, token_major, world)
 
     def step(self, stream=None, events=None):
         self.chain.run_device(self.w, self.ids, self.q, self.k, self.o, self.gate, self.up, self.h, self.n1,
@@ -309,10 +345,10 @@ class Chain:
         ms = t0.elapsed_time(t1) / steps
         return ms, h2d, d2h, launches
 
-    # -- the oracle on a bounded sample of the same pass (one Q/K batch = 4096 tokens)
-    @staticmethod
-    def cpu_sample(min_seconds=8.0, max_reps=50):
-        c = CpuChain()
+    # -- the oracle on the same pass (rank 0's shard), a bounded number of passes
+    def cpu_sample(self, min_seconds=8.0, max_reps=50):
+        c = CpuChain(self.tokens, self.token_major)
+        c.run_once()  # first touch of the outputs
         reps, t0 = 0, time.perf_counter()
         while True:
             c.run_once()
@@ -322,46 +358,71 @@ class Chain:
                 break
         sec = el / reps
         return {"gbs": c.bytes / sec / 1e9, "sec_per_sample": sec, "cores": c.cores,
-                "sample": f"{c.tokens} tokens of the chain (one Q/K batch [1, 16, 4096, 128]), {reps} reps, "
+                "sample": f"{reps} whole passes of the {c.tokens}-token chain (rank 0's inputs), "
                           f"oracle with {c.cores} OpenMP threads"}
 
 
-class CpuChain:
-    """The chained pass on the host through the oracle (the reference's path,
-    restated in C), on a bounded sample: one Q/K batch of 4096 tokens."""
+def synth_tag(name):
+    """The counter-based generator's 32-bit tensor tag (crc32 of the name)."""
+    import zlib
 
-    def __init__(self):
+    return zlib.crc32(name.encode())
+
+
+class CpuChain:
+    """The chained pass on the host cores through the oracle (a C restatement
+    of the reference's kernels, all OpenMP threads): the same workload as the
+    GPU arm -- `tokens` tokens of rank 0's counter-based inputs, in the same
+    Q/K layout -- with every output buffer allocated once and RoPE in place,
+    as the reference's kernels run.  Imports nothing of the library."""
+
+    def __init__(self, tokens=CHAIN_B * CHAIN_S, token_major=True):
+        import ctypes
+
         import numpy as np
 
         sys.path.insert(0, ROOT)
-        from oracle import Oracle, f32_to_bf16
-        from hrm_layer_ops.chain import algorithmic_bytes_per_token
+        from oracle import Oracle
 
+        if tokens % CHAIN_S or tokens <= 0:
+            raise SystemExit(f"--tokens must be a positive multiple of {CHAIN_S}")
         self.o = o = Oracle()
         # all the host cores this process may use (torchrun exports OMP_NUM_THREADS=1)
         o.set_threads(len(os.sched_getaffinity(0)))
-        rng = np.random.default_rng(0)
-        self.tokens = T = CHAIN_S
-
-        def nb(shape, std=1.0, mean=0.0):
-            return f32_to_bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(std) + np.float32(mean))
-
-        self.table = nb((VOCAB, HIDDEN), 0.02)
-        self.w1, self.w2 = nb(HIDDEN, 0.1, 1.0), nb(HIDDEN, 0.1, 1.0)
-        self.rope = o.rope_table(CHAIN_S, HEAD_DIM, THETA)
-        self.ids = rng.integers(0, VOCAB, T, dtype=np.uint32)
-        self.q, self.k = nb((1, HEADS, CHAIN_S, HEAD_DIM)), nb((1, HEADS, CHAIN_S, HEAD_DIM))
-        self.ob = nb((T, HIDDEN))
-        self.g, self.u = nb((T, INTER), 0.5), nb((T, INTER), 0.5)
-        self.bytes = algorithmic_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)["minimal"] * T
         self.cores = o.max_threads()
+        self.tokens = T = tokens
+        self.token_major = token_major
+        u16 = np.uint16
+
+        def nb(name, shape, start=0, std=1.0, mean=0.0):
+            return o.fill_normal_bf16(np.empty(shape, u16), SEED, synth_tag(name), start, std, mean)
+
+        self.table = nb("embed_table", (VOCAB, HIDDEN), std=0.02)
+        self.w1 = nb("norm1_weight", (HIDDEN,), std=0.1, mean=1.0)
+        self.w2 = nb("norm2_weight", (HIDDEN,), std=0.1, mean=1.0)
+        self.rope = o.rope_table(CHAIN_S, HEAD_DIM, THETA)
+        self.ids = o.fill_ids(np.empty(T, np.uint32), SEED, synth_tag("ids"), VOCAB)
+        self.qk_shape = chain_qk_shape(T, token_major)
+        self.q, self.k = nb("q", self.qk_shape), nb("k", self.qk_shape)
+        self.ob = nb("attn_out", (T, HIDDEN))
+        self.g, self.u = nb("gate", (T, INTER), std=0.5), nb("up", (T, INTER), std=0.5)
+        self.h, self.n1, self.r, self.n2 = (np.empty((T, HIDDEN), u16) for _ in range(4))
+        self.y = np.empty((T, INTER), u16)
+        self.bytes = chain_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)["minimal"] * T
+        p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+        self._p = {n: p(getattr(self, n)) for n in ("table", "w1", "w2", "rope", "ids", "q", "k", "ob", "g", "u",
+                                                     "h", "n1", "r", "n2", "y")}
 
     def run_once(self):
-        o = self.o
-        h, _ = o.embed_rms_norm(self.ids, self.table, SCALE, self.w1, EPS)
-        o.rope_embed(self.q, self.k, 0, THETA, self.rope)
-        o.add_rms_norm(h, self.ob, self.w2, EPS)
-        o.swiglu_ffn(self.g, self.u)
+        lib, p, T = self.o.lib, self._p, self.tokens
+        lib.ora_embed_rms_norm(p["ids"], p["table"], p["h"], p["n1"], p["w1"], T, HIDDEN, VOCAB, SCALE, EPS)
+        B = T // CHAIN_S
+        if self.token_major:
+            lib.ora_rope_embed_token_major(p["q"], p["k"], B, CHAIN_S, HEADS, HEAD_DIM, 0, THETA, p["rope"])
+        else:
+            lib.ora_rope_embed(p["q"], p["k"], B, HEADS, CHAIN_S, HEAD_DIM, 0, THETA, p["rope"])
+        lib.ora_add_rms_norm(p["h"], p["ob"], p["r"], p["n2"], p["w2"], T, HIDDEN, EPS)
+        lib.ora_swiglu_ffn(p["g"], p["u"], p["y"], T * INTER)
 
 
 class SingleOp:
@@ -585,14 +646,17 @@ class Module:
 
 
 # ------------------------------------------------------------------ main
-def reference_arm(args, rank):
-    """The reference's path on the host cores: the oracle, all threads."""
+def reference_arm(args, world, rank):
+    """The reference's path on the host cores: the oracle, all threads, over the
+    whole pass of the GPU arm's workload (rank 0's shard of --tokens tokens).
+    Imports nothing of the library (neither hrm_layer_ops nor libhrm_ops.so)."""
     if rank != 0:
         return
     if args.workload != "chain":
         print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the chain workload"}))
         return
-    c = CpuChain()
+    token_major = args.qk_layout == "token"
+    c = CpuChain(args.tokens, token_major)
     for _ in range(args.warmup):
         c.run_once()
     t0 = time.perf_counter()
@@ -600,22 +664,18 @@ def reference_arm(args, rank):
         c.run_once()
     sec = (time.perf_counter() - t0) / args.steps
     gbs = c.bytes / sec / 1e9
-    from hrm_layer_ops.chain import algorithmic_bytes_per_token
-
-    tokens = CHAIN_S
+    sample = (f"whole {c.tokens}-token passes of the chain (rank 0's counter-based inputs, "
+              f"{'token' if token_major else 'head'}-major Q/K), oracle with {c.cores} OpenMP threads")
     line = {
-        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1000, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 math)",
-        "data": "synthetic (seeded numpy, host)",
-        "config": {"workload": "chain: embed+RMSNorm -> RoPE -> add+RMSNorm -> SwiGLU",
-                   "tokens_per_step": tokens, "hidden": HIDDEN, "intermediate": INTER,
-                   "bytes_per_token_minimal": algorithmic_bytes_per_token(HIDDEN, HEADS, HEAD_DIM, INTER)["minimal"],
-                   "note": "each step is a bounded sample (4096 tokens) of the 65536-token pass"},
-        "rows_per_s": round(tokens / sec, 1),
+        "data": "synthetic, counter-based (splitmix64 + Box-Muller keyed by seed, tensor and global index), "
+                "generated on the host by the oracle; the same values as the GPU arm's rank 0",
+        "config": chain_config(c.tokens, token_major, world),
+        "rows_per_s": round(c.tokens / sec, 1),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": c.cores, "kind": "port",
-                         "sample": f"{c.tokens} tokens of the chain (one Q/K batch [1, 16, 4096, 128]) per step, "
-                                   f"oracle with {c.cores} OpenMP threads"},
+                         "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -627,7 +687,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        reference_arm(args, rank)
+        reference_arm(args, world, rank)
         return
 
     import datetime
@@ -665,7 +725,7 @@ def run_ours(args, world, rank, device, peers):
             peers.sync(phase, timeout_s=120)
 
     if args.workload == "chain":
-        wl = Chain(device, rank, args.tokens, args.qk_layout == "token", args.chunk_tokens)
+        wl = Chain(device, rank, world, args.tokens, args.qk_layout == "token", args.chunk_tokens)
     elif args.workload == "module":
         wl = Module(device, rank)
     else:
@@ -744,7 +804,7 @@ def run_ours(args, world, rank, device, peers):
                                                       "(public API)")}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and isinstance(wl, Chain):
-        c = Chain.cpu_sample()
+        c = wl.cpu_sample()
         cpu = {"value": round(c["gbs"], 3), "unit": "GB/s", "cores": c["cores"], "kind": "port",
                "sample": c["sample"]}
 
@@ -763,7 +823,7 @@ def run_ours(args, world, rank, device, peers):
         "metric": METRIC, "value": round(value_gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16 (fp32 math)", "data": getattr(wl, "data", "synthetic (seeded, generated on device)"),
-        "config": dict(wl.config, parallelism=f"{world} row shards, no collective"),
+        "config": wl.config if isinstance(wl, Chain) else dict(wl.config, parallelism=f"{world} row shards, no collective"),
         "pct_of_peak": round(100 * value_gbs / (world * peak), 2), "rows_per_s": round(rows_per_s, 1),
         "effective_gbs": round(world * wl.footprint / (ms_step / 1e3) / 1e9, 3),
         "per_kernel": {k: {"us": round(kern_ms[k] * 1e3, 2),

@@ -167,7 +167,8 @@ int rope_common(void* q, void* k, int64_t batch_size, int64_t num_heads, int64_t
   if (batch_size < 0 || num_heads < 0 || seq_len < 0 || head_dim <= 0 || head_dim % 2 != 0 ||
       position_offset < 0 || num_heads > INT32_MAX || head_dim > INT32_MAX)
     return HRM_ERR_INVALID_SHAPE;
-  if (position_offset + seq_len > INT32_MAX) return HRM_ERR_SIZE_OVERFLOW;
+  // offset + seq <= INT32_MAX, checked without forming a sum that could overflow
+  if (seq_len > INT32_MAX || position_offset > INT32_MAX - seq_len) return HRM_ERR_SIZE_OVERFLOW;
   if (batch_size == 0 || num_heads == 0 || seq_len == 0) return HRM_OK;
   if (!q || !k) return HRM_ERR_NULL_POINTER;
   const int64_t bytes = mul_checked(mul_checked(mul_checked(mul_checked(batch_size, num_heads), seq_len), head_dim), 2);
@@ -254,10 +255,12 @@ int hrm_split_gqkv_rope(const void* gqkv, void* gate_out, void* q_out, void* k_o
   if (batch_size < 0 || num_heads < 0 || seq_len < 0 || head_dim <= 0 || head_dim % 2 != 0 ||
       position_offset < 0 || cache_offset < 0 || num_heads > INT32_MAX || head_dim > INT32_MAX)
     return HRM_ERR_INVALID_SHAPE;
-  if (position_offset + seq_len > INT32_MAX) return HRM_ERR_SIZE_OVERFLOW;
+  // offset + seq <= INT32_MAX, checked without forming a sum that could overflow
+  if (seq_len > INT32_MAX || position_offset > INT32_MAX - seq_len) return HRM_ERR_SIZE_OVERFLOW;
   if ((k_cache == nullptr) != (v_cache == nullptr)) return HRM_ERR_NULL_POINTER;
   const bool cache = k_cache != nullptr;
-  if (cache && (cache_len < 0 || cache_offset + seq_len > cache_len)) return HRM_ERR_INVALID_SHAPE;
+  if (cache && (cache_len < 0 || seq_len > cache_len || cache_offset > cache_len - seq_len))
+    return HRM_ERR_INVALID_SHAPE;
   if (batch_size == 0 || num_heads == 0 || seq_len == 0) return HRM_OK;
   if (!gqkv || !gate_out || !q_out || !k_out || !v_out) return HRM_ERR_NULL_POINTER;
   const int64_t bytes = mul_checked(mul_checked(mul_checked(mul_checked(batch_size, num_heads), seq_len), head_dim), 2);

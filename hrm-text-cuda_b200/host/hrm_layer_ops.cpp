@@ -25,12 +25,15 @@ void need(const CudaSlice<T>& s, size_t elems, const char* op, const char* name)
 
 }  // namespace
 
+// half 2.7.1's bf16::from_f32, the conversion the reference's host code uses:
+// round to nearest even; a NaN keeps its sign and high payload bits and is
+// made quiet (0x0040), as the GPU loader conversion (hrm_convert_to_bf16) does.
 bf16 bf16::from_f32(float f) {
   uint32_t u;
   std::memcpy(&u, &f, 4);
   bf16 r;
   if ((u & 0x7fffffffu) > 0x7f800000u) {
-    r.bits = 0x7fffu;
+    r.bits = (uint16_t)((u >> 16) | 0x0040u);
   } else {
     u += 0x7fffu + ((u >> 16) & 1u);
     r.bits = (uint16_t)(u >> 16);

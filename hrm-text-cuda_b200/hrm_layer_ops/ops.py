@@ -1,9 +1,11 @@
 """PyTorch-tensor front end of the C ABI (one function per hrm_* entry point).
 
 Tensors supply device memory and the stream; every operator runs in
-libhrm_ops.so.  Inputs must be contiguous CUDA tensors; a CPU tensor is an
-error, never a silent fallback.  By default work is queued on the current
-torch stream of the tensors' device.
+libhrm_ops.so.  Inputs must be contiguous CUDA tensors, all on one device; a
+CPU tensor, or a tensor on another GPU, is an error, never a silent fallback.
+The launch runs with that device current (the library sizes its grids from
+the current device and launches there), by default on its current torch
+stream.
 """
 
 from __future__ import annotations
@@ -27,6 +29,22 @@ def _stream(t: torch.Tensor, stream: Optional[torch.cuda.Stream]) -> ctypes.c_vo
     return _vp(s.cuda_stream)
 
 
+def _launch(name: str, tensors, stream: Optional[torch.cuda.Stream], *args) -> None:
+    """Calls `name` with `args` and the stream, with the device of `tensors`
+    current.  Every tensor (None entries skipped) must be on that one device,
+    and so must an explicit stream: a pointer into another GPU's memory would
+    reach the kernel as an illegal address."""
+    ts = [t for t in tensors if t is not None]
+    dev = ts[0].device
+    for t in ts[1:]:
+        if t.device != dev:
+            raise ValueError(f"{name}: tensors on {dev} and {t.device}; every argument must be on one device")
+    if stream is not None and stream.device != dev:
+        raise ValueError(f"{name}: stream on {stream.device} but tensors on {dev}")
+    with torch.cuda.device(dev):
+        call(name, *args, _stream(ts[0], stream))
+
+
 def _need(t: torch.Tensor, name: str, dtypes=(torch.bfloat16,)) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
@@ -39,6 +57,9 @@ def _need(t: torch.Tensor, name: str, dtypes=(torch.bfloat16,)) -> None:
 
 
 def _ids(t: torch.Tensor, name: str) -> None:
+    """Token ids: uint32 (the reference's type) or int32 read as uint32, so a
+    negative int32 id is a huge uint32 and clamps to vocab - 1 like any id at
+    or beyond the vocabulary (src/kernels/embedding_lookup.cu:35)."""
     _need(t, name, (torch.int32, torch.uint32))
 
 
@@ -52,7 +73,7 @@ def additive_inject(z_a: torch.Tensor, z_b: torch.Tensor, out: Optional[torch.Te
     _need(out, "out")
     if out.numel() != z_a.numel():
         raise ValueError("out has the wrong size")
-    call("hrm_additive_inject", _ptr(z_a), _ptr(z_b), _ptr(out), z_a.numel(), _stream(z_a, stream))
+    _launch("hrm_additive_inject", (z_a, z_b, out), stream, _ptr(z_a), _ptr(z_b), _ptr(out), z_a.numel())
     return out
 
 
@@ -66,7 +87,7 @@ def swiglu_ffn(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor]
     _need(out, "out")
     if out.numel() != gate.numel():
         raise ValueError("out has the wrong size")
-    call("hrm_swiglu_ffn", _ptr(gate), _ptr(up), _ptr(out), gate.numel(), _stream(gate, stream))
+    _launch("hrm_swiglu_ffn", (gate, up, out), stream, _ptr(gate), _ptr(up), _ptr(out), gate.numel())
     return out
 
 
@@ -92,7 +113,7 @@ def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None, eps: float 
     if out.numel() != x.numel():
         raise ValueError("out has the wrong size")
     fn = "hrm_rms_norm" if x.dtype == torch.bfloat16 else "hrm_rms_norm_f32"
-    call(fn, _ptr(x), _ptr(out), _ptr(weight), rows, hidden, eps, _stream(x, stream))
+    _launch(fn, (x, weight, out), stream, _ptr(x), _ptr(out), _ptr(weight), rows, hidden, eps)
     return out
 
 
@@ -116,8 +137,8 @@ def add_rms_norm(x: torch.Tensor, branch: torch.Tensor, weight: Optional[torch.T
     _need(residual_out, "residual_out"); _need(normed_out, "normed_out")
     if residual_out.numel() != x.numel() or normed_out.numel() != x.numel():
         raise ValueError("outputs have the wrong size")
-    call("hrm_add_rms_norm", _ptr(x), _ptr(branch), _ptr(residual_out), _ptr(normed_out), _ptr(weight), rows,
-         hidden, eps, _stream(x, stream))
+    _launch("hrm_add_rms_norm", (x, branch, weight, residual_out, normed_out), stream, _ptr(x), _ptr(branch),
+            _ptr(residual_out), _ptr(normed_out), _ptr(weight), rows, hidden, eps)
     return residual_out, normed_out
 
 
@@ -131,7 +152,7 @@ def rope_table(max_positions: int, head_dim: int, theta: float = 10000.0,
     _need(out, "out", (torch.float32,))
     if out.numel() != max_positions * head_dim:
         raise ValueError("out has the wrong size")
-    call("hrm_rope_table_build", _ptr(out), max_positions, head_dim, theta, _stream(out, stream))
+    _launch("hrm_rope_table_build", (out,), stream, _ptr(out), max_positions, head_dim, theta)
     return out
 
 
@@ -152,8 +173,8 @@ def rope_embed(q: torch.Tensor, k: torch.Tensor, position_offset: int = 0, theta
         if table.dim() != 2 or table.shape[1] != d:
             raise ValueError("table must be [positions, head_dim]")
         positions = table.shape[0]
-    call("hrm_rope_embed", _ptr(q), _ptr(k), b, h, s, d, position_offset, theta, _ptr(table), positions,
-         _stream(q, stream))
+    _launch("hrm_rope_embed", (q, k, table), stream, _ptr(q), _ptr(k), b, h, s, d, position_offset, theta,
+            _ptr(table), positions)
     return q, k
 
 
@@ -170,8 +191,8 @@ def rope_embed_token_major(q: torch.Tensor, k: torch.Tensor, position_offset: in
         if table.dim() != 2 or table.shape[1] != d:
             raise ValueError("table must be [positions, head_dim]")
         positions = table.shape[0]
-    call("hrm_rope_embed_token_major", _ptr(q), _ptr(k), b, s, h, d, position_offset, theta, _ptr(table),
-         positions, _stream(q, stream))
+    _launch("hrm_rope_embed_token_major", (q, k, table), stream, _ptr(q), _ptr(k), b, s, h, d, position_offset,
+            theta, _ptr(table), positions)
     return q, k
 
 
@@ -186,8 +207,8 @@ def embedding_lookup(ids: torch.Tensor, table: torch.Tensor, embedding_scale: fl
     _need(out, "out")
     if out.numel() != ids.numel() * hidden:
         raise ValueError("out has the wrong size")
-    call("hrm_embedding_lookup", _ptr(ids), _ptr(table), _ptr(out), 1, ids.numel(), hidden, vocab,
-         embedding_scale, _stream(table, stream))
+    _launch("hrm_embedding_lookup", (table, ids, out), stream, _ptr(ids), _ptr(table), _ptr(out), 1, ids.numel(),
+            hidden, vocab, embedding_scale)
     return out
 
 
@@ -212,8 +233,8 @@ def embed_rms_norm(ids: torch.Tensor, table: torch.Tensor, embedding_scale: floa
         _need(weight, "weight")
         if weight.numel() != hidden:
             raise ValueError("weight must have hidden_size elements")
-    call("hrm_embed_rms_norm", _ptr(ids), _ptr(table), _ptr(hidden_out), _ptr(normed_out), _ptr(weight),
-         ids.numel(), hidden, vocab, embedding_scale, eps, _stream(table, stream))
+    _launch("hrm_embed_rms_norm", (table, ids, weight, hidden_out, normed_out), stream, _ptr(ids), _ptr(table),
+            _ptr(hidden_out), _ptr(normed_out), _ptr(weight), ids.numel(), hidden, vocab, embedding_scale, eps)
     return hidden_out, normed_out
 
 
@@ -248,9 +269,9 @@ def split_gqkv_rope(gqkv: torch.Tensor, num_heads: int, position_offset: int = 0
         if k_cache.dim() != 4 or k_cache.shape != v_cache.shape or k_cache.shape[:2] != (b, num_heads):
             raise ValueError("caches must be [batch, heads, cache_len, head_dim]")
         cache_len = k_cache.shape[2]
-    call("hrm_split_gqkv_rope", _ptr(gqkv), *(_ptr(t) for t in out), _ptr(k_cache), _ptr(v_cache), b, s,
-         num_heads, d, position_offset, theta, _ptr(table), positions, cache_len, cache_offset,
-         _stream(gqkv, stream))
+    _launch("hrm_split_gqkv_rope", (gqkv, *out, table, k_cache, v_cache), stream, _ptr(gqkv),
+            *(_ptr(t) for t in out), _ptr(k_cache), _ptr(v_cache), b, s, num_heads, d, position_offset, theta,
+            _ptr(table), positions, cache_len, cache_offset)
     return out
 
 
@@ -262,7 +283,8 @@ def gated_attn_output(gate: torch.Tensor, attn_out: torch.Tensor, out: Optional[
         raise ValueError("gate and attn_out differ in size")
     out = torch.empty_like(attn_out) if out is None else out
     _need(out, "out")
-    call("hrm_gated_attn_output", _ptr(gate), _ptr(attn_out), _ptr(out), gate.numel(), _stream(gate, stream))
+    _launch("hrm_gated_attn_output", (gate, attn_out, out), stream, _ptr(gate), _ptr(attn_out), _ptr(out),
+            gate.numel())
     return out
 
 
@@ -271,7 +293,7 @@ def apply_attn_gate(gate: torch.Tensor, attn_out: torch.Tensor, *, stream=None) 
     _need(gate, "gate"); _need(attn_out, "attn_out")
     if gate.numel() != attn_out.numel():
         raise ValueError("gate and attn_out differ in size")
-    call("hrm_apply_attn_gate", _ptr(gate), _ptr(attn_out), gate.numel(), _stream(gate, stream))
+    _launch("hrm_apply_attn_gate", (gate, attn_out), stream, _ptr(gate), _ptr(attn_out), gate.numel())
     return attn_out
 
 
@@ -283,7 +305,7 @@ def broadcast_vec(src: torch.Tensor, n_copies: int, out: Optional[torch.Tensor] 
     _need(out, "out")
     if out.numel() != n_copies * src.numel():
         raise ValueError("out has the wrong size")
-    call("hrm_broadcast_vec", _ptr(out), _ptr(src), n_copies, src.numel(), _stream(src, stream))
+    _launch("hrm_broadcast_vec", (src, out), stream, _ptr(out), _ptr(src), n_copies, src.numel())
     return out
 
 
@@ -302,7 +324,7 @@ def convert_to_bf16(raw: torch.Tensor, dtype: str, out: Optional[torch.Tensor] =
     _need(out, "out")
     if out.numel() != n:
         raise ValueError("out has the wrong size")
-    call("hrm_convert_to_bf16", _ptr(raw), DTYPES[dtype], _ptr(out), n, _stream(raw, stream))
+    _launch("hrm_convert_to_bf16", (raw, out), stream, _ptr(raw), DTYPES[dtype], _ptr(out), n)
     return out
 
 

@@ -4,6 +4,8 @@ and the CPU-baseline legs of bench.py."""
 
 from .oracle import (  # noqa: F401
     Oracle,
+    REF_LIB,
+    REF_LIB_PTX,
     RefKernels,
     bf16_to_f32,
     bf16_ulp,

@@ -193,32 +193,46 @@ static float rot_lo(float x0, float x1, float c, float s) { return fmaf(x0, c, -
 static float rot_hi_q(float x0, float x1, float c, float s) { return fmaf(x1, c, x0 * s); }
 static float rot_hi_k(float x0, float x1, float c, float s) { return fmaf(x0, s, x1 * c); }
 
-/* rope_embed.cu:27-53: pair (i, i + D/2) of row (b, h, s), Q then K. */
+/* rope_embed.cu:27-53: the pairs (i, i + D/2) of one head row of q and of k
+ * at position pos, Q then K. */
+static void rope_rows(uint16_t* qr, uint16_t* kr, int pos, int64_t head_dim, float theta, const float* table) {
+  const int64_t half = head_dim / 2;
+  for (int64_t i = 0; i < half; ++i) {
+    float c, s;
+    if (table) {
+      c = table[(int64_t)pos * head_dim + i];
+      s = table[(int64_t)pos * head_dim + half + i];
+    } else {
+      const float a = rope_angle(pos, (int)i, (int)head_dim, theta);
+      c = cosf(a);
+      s = sinf(a);
+    }
+    const float x0 = ora_bf16_to_f32(qr[i]), x1 = ora_bf16_to_f32(qr[i + half]);
+    qr[i] = ora_f32_to_bf16(rot_lo(x0, x1, c, s));
+    qr[i + half] = ora_f32_to_bf16(rot_hi_q(x0, x1, c, s));
+    const float k0 = ora_bf16_to_f32(kr[i]), k1 = ora_bf16_to_f32(kr[i + half]);
+    kr[i] = ora_f32_to_bf16(rot_lo(k0, k1, c, s));
+    kr[i + half] = ora_f32_to_bf16(rot_hi_k(k0, k1, c, s));
+  }
+}
+
+/* [B, H, S, D] (rope_embed.cu:35): row (b, h, s) is at position s + offset. */
 void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                     int64_t offset, float theta, const float* table) {
-  const int64_t half = head_dim / 2, rows = batch * heads * seq;
+  const int64_t rows = batch * heads * seq;
 #pragma omp parallel for schedule(static)
-  for (int64_t row = 0; row < rows; ++row) {
-    const int pos = (int)(row % seq) + (int)offset;
-    for (int64_t i = 0; i < half; ++i) {
-      float c, s;
-      if (table) {
-        c = table[(int64_t)pos * head_dim + i];
-        s = table[(int64_t)pos * head_dim + half + i];
-      } else {
-        const float a = rope_angle(pos, (int)i, (int)head_dim, theta);
-        c = cosf(a);
-        s = sinf(a);
-      }
-      const int64_t i0 = row * head_dim + i, i1 = i0 + half;
-      const float x0 = ora_bf16_to_f32(q[i0]), x1 = ora_bf16_to_f32(q[i1]);
-      q[i0] = ora_f32_to_bf16(rot_lo(x0, x1, c, s));
-      q[i1] = ora_f32_to_bf16(rot_hi_q(x0, x1, c, s));
-      const float k0 = ora_bf16_to_f32(k[i0]), k1 = ora_bf16_to_f32(k[i1]);
-      k[i0] = ora_f32_to_bf16(rot_lo(k0, k1, c, s));
-      k[i1] = ora_f32_to_bf16(rot_hi_k(k0, k1, c, s));
-    }
-  }
+  for (int64_t row = 0; row < rows; ++row)
+    rope_rows(q + row * head_dim, k + row * head_dim, (int)(row % seq) + (int)offset, head_dim, theta, table);
+}
+
+/* The same rotation over [B, S, H, D]: row (b, s, h) is at position s + offset. */
+void ora_rope_embed_token_major(uint16_t* q, uint16_t* k, int64_t batch, int64_t seq, int64_t heads,
+                                int64_t head_dim, int64_t offset, float theta, const float* table) {
+  const int64_t rows = batch * seq * heads;
+#pragma omp parallel for schedule(static)
+  for (int64_t row = 0; row < rows; ++row)
+    rope_rows(q + row * head_dim, k + row * head_dim, (int)((row / heads) % seq) + (int)offset, head_dim, theta,
+              table);
 }
 
 /* split_gqkv.cu:27-48 */
@@ -301,4 +315,44 @@ void ora_convert_to_bf16(const void* src, int dtype, uint16_t* dst, int64_t n) {
       dst[i] = dtype == 2 ? half_f32_to_bf16(half_f16_to_f32(h)) : h;
     }
   }
+}
+
+/* ------------------------------------------------ counter-based inputs
+ * The benchmark's synthetic inputs (the library's synth module restates the
+ * same scheme for numpy and torch): every element is a function of (seed,
+ * tensor tag, global index) alone, through the SplitMix64 finaliser:
+ *   key    = mix(seed * 0x9E3779B97F4A7C15 + tag)
+ *   bits_i = mix(key ^ mix(i))
+ *   normal : u = ((bits >> 11) + 1) * 2^-53 from i = 2j and 2j + 1;
+ *            z = sqrt(-2 ln u1) cos(2 pi u2) in double (Box-Muller);
+ *            value = bf16_rne(f32_rne(mean + std * z))
+ *   ids    : bits_i mod vocab */
+static uint64_t sm64_mix(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+static const double kPi = 3.14159265358979323846; /* the double nearest pi */
+
+static double sm64_unit(uint64_t b) { return ((double)(b >> 11) + 1.0) * 0x1p-53; }
+
+void ora_fill_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, uint64_t tag, int64_t start, double std_,
+                          double mean) {
+  const uint64_t key = sm64_mix(seed * 0x9E3779B97F4A7C15ull + tag);
+#pragma omp parallel for schedule(static)
+  for (int64_t j = 0; j < n; ++j) {
+    const uint64_t i = 2 * (uint64_t)(start + j);
+    const double u1 = sm64_unit(sm64_mix(key ^ sm64_mix(i)));
+    const double u2 = sm64_unit(sm64_mix(key ^ sm64_mix(i + 1)));
+    const double z = sqrt(-2.0 * log(u1)) * cos(2.0 * kPi * u2);
+    out[j] = ora_f32_to_bf16((float)(mean + std_ * z));
+  }
+}
+
+void ora_fill_ids(uint32_t* out, int64_t n, uint64_t seed, uint64_t tag, int64_t start, uint32_t vocab) {
+  const uint64_t key = sm64_mix(seed * 0x9E3779B97F4A7C15ull + tag);
+#pragma omp parallel for schedule(static)
+  for (int64_t j = 0; j < n; ++j) out[j] = (uint32_t)(sm64_mix(key ^ sm64_mix((uint64_t)(start + j))) % vocab);
 }

@@ -57,6 +57,9 @@ void ora_embed_rms_norm(const uint32_t* ids, const uint16_t* table, uint16_t* hi
 void ora_rope_table(float* table, int64_t positions, int64_t head_dim, float theta);
 void ora_rope_embed(uint16_t* q, uint16_t* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                     int64_t offset, float theta, const float* table);
+/* The same rotation over token-major [batch, seq, heads, head_dim] rows. */
+void ora_rope_embed_token_major(uint16_t* q, uint16_t* k, int64_t batch, int64_t seq, int64_t heads,
+                                int64_t head_dim, int64_t offset, float theta, const float* table);
 
 /* apply_attn_gate.cu:28-29 / gated_attn_output.cu:71-72:
  * out = (1 / (1 + exp(-g))) * a (expf in place of the __expf intrinsic). */
@@ -81,6 +84,13 @@ void ora_split_gqkv(const uint16_t* gqkv, uint16_t* gate, uint16_t* q, uint16_t*
 void ora_kv_cache_update(const uint16_t* k, const uint16_t* v, uint16_t* k_cache, uint16_t* v_cache, int64_t batch,
                          int64_t heads, int64_t seq, int64_t head_dim, int64_t max_len, int64_t cached_len,
                          int is_decode);
+
+/* Counter-based synthetic inputs (SplitMix64 + Box-Muller keyed by seed,
+ * tensor tag and global element index): normal bf16 values and token ids of
+ * elements [start, start + n) of the (seed, tag) stream. */
+void ora_fill_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, uint64_t tag, int64_t start, double std_,
+                          double mean);
+void ora_fill_ids(uint32_t* out, int64_t n, uint64_t seed, uint64_t tag, int64_t start, uint32_t vocab);
 
 #ifdef __cplusplus
 }

@@ -3,8 +3,10 @@
 * `Oracle`: numpy front end of liboracle.so, the CPU restatement of the
   reference kernels (hrm_oracle.c).  bf16 arrays are numpy uint16 bit patterns.
 * `RefKernels`: the reference's own src/kernels/*.cu, compiled from source for
-  sm_100a into _ref/libref_kernels.so and launched with the reference's launch
-  configurations (ref_launch.cu); takes torch CUDA tensors.
+  sm_100a into _ref/libref_kernels.so (or, as the reference ships them, as
+  compute_80 PTX that the driver compiles at load time, _ref/libref_kernels_ptx.so)
+  and launched with the reference's launch configurations (ref_launch.cu);
+  takes torch CUDA tensors.
 * numpy helpers for bf16 conversion and ulp measurement used by the tests.
 """
 
@@ -19,6 +21,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(HERE, "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libref_kernels.so")
+# The same kernels as the reference ships them: compute_80 PTX, compiled by the
+# driver for the GPU when the library loads.
+REF_LIB_PTX = os.path.join(HERE, "_ref", "libref_kernels_ptx.so")
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -85,6 +90,10 @@ class Oracle:
         "ora_broadcast_vec": [_p, _p, _i64, _i64],
         "ora_convert_to_bf16": [_p, ctypes.c_int, _p, _i64],
         "ora_set_threads": [ctypes.c_int],
+        "ora_rope_embed_token_major": [_p, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p],
+        "ora_fill_normal_bf16": [_p, _i64, ctypes.c_uint64, ctypes.c_uint64, _i64, ctypes.c_double,
+                                 ctypes.c_double],
+        "ora_fill_ids": [_p, _i64, ctypes.c_uint64, ctypes.c_uint64, _i64, ctypes.c_uint32],
     }
 
     def __init__(self, path: str = ORACLE_LIB):
@@ -168,11 +177,33 @@ class Oracle:
 
     def rope_embed(self, q, k, offset=0, theta=10000.0, table=None):
         """Returns rotated copies of q, k ([B, H, S, D] uint16)."""
-        q, k = np.array(q, dtype=np.uint16, copy=True), np.array(k, dtype=np.uint16, copy=True)
+        q, k = (np.array(a, dtype=np.uint16, order="C", copy=True) for a in (q, k))
         table = self._c(table, np.float32)
         b, h, s, d = q.shape
         self.lib.ora_rope_embed(self._ptr(q), self._ptr(k), b, h, s, d, offset, theta, self._ptr(table))
         return q, k
+
+    def rope_embed_token_major(self, q, k, offset=0, theta=10000.0, table=None):
+        """Returns rotated copies of q, k ([B, S, H, D] uint16)."""
+        q, k = (np.array(a, dtype=np.uint16, order="C", copy=True) for a in (q, k))
+        table = self._c(table, np.float32)
+        b, s, h, d = q.shape
+        self.lib.ora_rope_embed_token_major(self._ptr(q), self._ptr(k), b, s, h, d, offset, theta,
+                                            self._ptr(table))
+        return q, k
+
+    def fill_normal_bf16(self, out, seed, tag, start=0, std=1.0, mean=0.0):
+        """Fills the contiguous uint16 array `out` with elements [start, start + out.size)
+        of the counter-based (seed, tag) normal stream, as bf16 bits."""
+        assert out.dtype == np.uint16 and out.flags.c_contiguous
+        self.lib.ora_fill_normal_bf16(self._ptr(out), out.size, seed, tag, start, std, mean)
+        return out
+
+    def fill_ids(self, out, seed, tag, vocab, start=0):
+        """Fills the contiguous uint32 array `out` with ids [start, start + out.size) of the stream."""
+        assert out.dtype == np.uint32 and out.flags.c_contiguous
+        self.lib.ora_fill_ids(self._ptr(out), out.size, seed, tag, start, vocab)
+        return out
 
 
     def gated_attn_output(self, gate, attn):
@@ -209,7 +240,7 @@ class Oracle:
     def kv_cache_update(self, k, v, k_cache, v_cache, cached_len, is_decode):
         """Writes into copies of the caches and returns them."""
         k, v = self._c(k, np.uint16), self._c(v, np.uint16)
-        kc, vc = np.array(k_cache, np.uint16, copy=True), np.array(v_cache, np.uint16, copy=True)
+        kc, vc = (np.array(a, np.uint16, order="C", copy=True) for a in (k_cache, v_cache))
         b, h, s, d = k.shape
         self.lib.ora_kv_cache_update(self._ptr(k), self._ptr(v), self._ptr(kc), self._ptr(vc), b, h, s, d,
                                      kc.shape[2], cached_len, int(is_decode))

@@ -3,7 +3,9 @@
 * `gpu` marker: tests that need a CUDA device (run with `-m gpu` on a B200).
 * Paths: the repo root (for the `oracle` checker package) and the library's
   Python front end (`hrm-text-cuda_b200/hrm_layer_ops`).
-* The oracle and the product library are built on first use if missing.
+* The product library and the oracle are (re)built before the tests run: make
+  is incremental, so a source edited since the last build is never tested
+  through a stale library.
 """
 
 import os
@@ -27,10 +29,8 @@ def pytest_configure(config):
 
 
 def _ensure_built():
-    if not os.path.exists(os.path.join(PKG, "lib", "libhrm_ops.so")):
-        subprocess.run(["make", "-C", PKG, "-s", "-j8"], check=True)
-    if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
-        subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "-s", "liboracle.so"], check=True)
+    subprocess.run(["make", "-C", PKG, "-s", "-j8"], check=True)
+    subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "-s", "liboracle.so"], check=True)
 
 
 _ensure_built()

@@ -2,10 +2,12 @@
 // tests (src/lib.rs:2225-2279: test_additive_inject, test_rms_norm,
 // test_swiglu_ffn) through HrmLayerOps, plus known answers for the two ops
 // the reference never tested (embedding_lookup, rope_embed) and the fused
-// entry points.  Needs a GPU; prints one line per test and exits non-zero on
-// the first failure.
+// entry points.  Needs a GPU, except with --host-only, which runs only the
+// tests of host code; prints one line per test and exits non-zero on the
+// first failure.
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <functional>
 #include <string>
 #include <vector>
@@ -31,6 +33,21 @@ struct Failure {
 
 void expect(bool ok, const std::string& what) {
   if (!ok) throw Failure{what};
+}
+
+// Host-side f32 -> bf16 (half 2.7.1's bf16::from_f32): RNE, and a NaN keeps its
+// sign and payload's high bits with the quiet bit set -- the same bits as the
+// GPU loader conversion.
+void test_bf16_from_f32() {
+  const uint32_t in[] = {0x3f800000u, 0x3f808000u, 0x3f818000u, 0x3f808001u, 0x7f800000u, 0xff800000u,
+                         0x7fc00000u, 0xffc00001u, 0x7f800001u, 0xff812345u, 0x00000001u, 0x7f7fffffu};
+  const uint16_t want[] = {0x3f80, 0x3f80, 0x3f82, 0x3f81, 0x7f80, 0xff80,
+                           0x7fc0, 0xffc0, 0x7fc0, 0xffc1, 0x0000, 0x7f80};
+  for (int i = 0; i < 12; ++i) {
+    float f;
+    std::memcpy(&f, &in[i], 4);
+    expect(bf16::from_f32(f).bits == want[i], "from_f32 case " + std::to_string(i));
+  }
 }
 
 // src/lib.rs:2227-2243
@@ -465,7 +482,23 @@ void test_recurrent_forward(HrmLayerOps&) {
 
 }  // namespace
 
-int main() {
+int main(int argc, char** argv) {
+  const std::vector<std::pair<const char*, std::function<void()>>> host_tests = {
+      {"test_bf16_from_f32", test_bf16_from_f32},
+  };
+  for (const auto& t : host_tests) {
+    try {
+      t.second();
+    } catch (const Failure& f) {
+      std::printf("FAIL %s: %s\n", t.first, f.what.c_str());
+      return 1;
+    }
+    std::printf("ok   %s\n", t.first);
+  }
+  if (argc > 1 && std::strcmp(argv[1], "--host-only") == 0) {
+    std::printf("all %zu host tests passed\n", host_tests.size());
+    return 0;
+  }
   const std::vector<std::pair<const char*, std::function<void(HrmLayerOps&)>>> tests = {
       {"test_additive_inject", test_additive_inject}, {"test_rms_norm", test_rms_norm},
       {"test_swiglu_ffn", test_swiglu_ffn},           {"test_embedding_lookup", test_embedding_lookup},

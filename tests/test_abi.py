@@ -139,6 +139,18 @@ def test_validation_rope_table_range_and_overflow(lib):
     assert lib.hrm_rope_embed(vp(A), vp(B), 1, 1, 2, 128, 2**31 - 1, 1e4, None, 0,
                               None) == _lib.HRM_ERR_SIZE_OVERFLOW
     assert lib.hrm_additive_inject(vp(A), vp(B), vp(C), 2**62, None) == _lib.HRM_ERR_SIZE_OVERFLOW
+    # offsets near INT64_MAX are rejected without forming an overflowing sum
+    big = 2**63 - 1
+    assert lib.hrm_rope_embed(vp(A), vp(B), 1, 1, 2, 128, big, 1e4, None, 0, None) == _lib.HRM_ERR_SIZE_OVERFLOW
+    assert lib.hrm_rope_embed(vp(A), vp(B), 1, 1, big, 128, 1, 1e4, None, 0, None) == _lib.HRM_ERR_SIZE_OVERFLOW
+    D = 0x40000000
+    split = lambda offset, cache_len, cache_offset: lib.hrm_split_gqkv_rope(  # noqa: E731
+        vp(A), vp(B), vp(C), vp(C + D), vp(C + 2 * D), vp(C + 3 * D), vp(C + 4 * D), 1, 2, 1, 128, offset, 1e4,
+        None, 0, cache_len, cache_offset, None)
+    assert split(big, 0, 0) == _lib.HRM_ERR_SIZE_OVERFLOW
+    assert split(0, 8, big) == _lib.HRM_ERR_INVALID_SHAPE  # cache_offset + seq would overflow
+    assert split(0, 8, 7) == _lib.HRM_ERR_INVALID_SHAPE    # rows 7 and 8 of an 8-row cache
+    assert split(0, 1, 0) == _lib.HRM_ERR_INVALID_SHAPE    # seq 2 > cache_len 1
 
 
 def test_front_end_rejects_cpu_tensors():
@@ -151,3 +163,30 @@ def test_front_end_rejects_cpu_tensors():
         hrm_layer_ops.rms_norm(x)
     with pytest.raises(ValueError, match="CUDA"):
         hrm_layer_ops.swiglu_ffn(x, x)
+
+
+def test_front_end_refuses_tensors_on_two_devices():
+    """Every tensor of a call (and an explicit stream) must be on one device:
+    checked on the host before the library is called."""
+    from types import SimpleNamespace
+
+    import torch
+
+    from hrm_layer_ops import ops
+
+    t0 = SimpleNamespace(device=torch.device("cuda", 0))
+    t1 = SimpleNamespace(device=torch.device("cuda", 1))
+    with pytest.raises(ValueError, match="one device"):
+        ops._launch("hrm_swiglu_ffn", (t0, None, t1), None)
+    with pytest.raises(ValueError, match="stream on"):
+        ops._launch("hrm_swiglu_ffn", (t0, t0), SimpleNamespace(device=torch.device("cuda", 1)))
+
+
+def test_cpp_host_conversions_without_a_gpu():
+    """The C++ host layer's own f32 -> bf16 (half's from_f32, NaN rule included)."""
+    import subprocess
+
+    exe = os.path.join(PKG, "build", "test_layer_ops")
+    res = subprocess.run([exe, "--host-only"], capture_output=True, text=True, timeout=60)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "all 1 host tests passed" in res.stdout

@@ -1,9 +1,11 @@
 """CPU: the benchmark's reference arm and its JSON line (no GPU needed).
 
 `bench.py --impl reference` times the reference's path restated on the host
-(the oracle) and prints exactly one JSON line with the metric, the CPU
-baseline and an e2e object; a workload it does not cover prints an
-`unavailable` line and exits 0.
+(the oracle) over whole passes of the GPU arm's workload and prints exactly
+one JSON line with the metric, the CPU baseline and an e2e object; a
+workload it does not cover prints an `unavailable` line and exits 0.  The arm
+loads nothing of the library: neither the hrm_layer_ops package nor
+libhrm_ops.so.
 """
 
 import json
@@ -23,7 +25,7 @@ def run_bench(*args, timeout=600):
 
 
 def test_reference_arm_prints_one_contract_line():
-    res, lines = run_bench("--impl", "reference", "--steps", "1", "--warmup", "3")
+    res, lines = run_bench("--impl", "reference", "--steps", "1", "--warmup", "3", "--tokens", "8192")
     assert res.returncode == 0, res.stderr[-2000:]
     assert len(lines) == 1, res.stdout[-2000:]
     d = json.loads(lines[0])
@@ -35,6 +37,49 @@ def test_reference_arm_prints_one_contract_line():
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert d["config"]["tokens_per_gpu"] == 8192 and d["config"]["qk_shape"] == [2, 4096, 16, 128]
+
+
+def test_reference_arm_defaults_to_the_whole_gpu_workload():
+    """Without --tokens both arms run the 65536-token pass, with the same config dict."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    old = sys.argv
+    try:
+        sys.argv = ["bench.py", "--impl", "reference"]
+        args = bench.parse_args()
+    finally:
+        sys.argv = old
+    assert args.tokens == 65536 and args.qk_layout == "token"
+    cfg = bench.chain_config(args.tokens, True, 1)
+    assert cfg["tokens_per_gpu"] == 65536 and cfg["qk_shape"] == [16, 4096, 16, 128]
+
+
+def test_reference_arm_loads_nothing_of_the_library():
+    code = (
+        "import sys, runpy\n"
+        "sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '3', '--tokens', '4096']\n"
+        "runpy.run_path('bench.py', run_name='__main__')\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print('LOADED', [m for m in sys.modules if m.startswith('hrm_layer_ops')], 'libhrm_ops' in maps,"
+        " 'liboracle' in maps)\n")
+    env = dict(os.environ, OMP_NUM_THREADS="4")
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, env=env,
+                         cwd=ROOT)
+    assert res.returncode == 0, res.stderr[-2000:]
+    last = [l for l in res.stdout.splitlines() if l.startswith("LOADED")][-1]
+    assert last == "LOADED [] False True", last
+
+
+def test_bench_byte_counts_equal_the_library_s():
+    sys.path.insert(0, ROOT)
+    import bench
+    from hrm_layer_ops.chain import CHAIN_KERNELS, algorithmic_bytes_per_token
+
+    assert tuple(bench.CHAIN_KERNEL_NAMES) == tuple(CHAIN_KERNELS)
+    for dims in ((2048, 16, 128, 5632), (1536, 12, 128, 4096), (64, 2, 16, 40)):
+        assert bench.chain_bytes_per_token(*dims) == algorithmic_bytes_per_token(*dims)
 
 
 def test_reference_arm_other_workload_is_unavailable():
@@ -51,7 +96,8 @@ def test_warmup_below_three_is_refused():
 
 
 def test_reference_arm_at_the_reference_model_dims():
-    res, lines = run_bench("--impl", "reference", "--dims", "hrm-text-1b", "--steps", "1", "--warmup", "3")
+    res, lines = run_bench("--impl", "reference", "--dims", "hrm-text-1b", "--steps", "1", "--warmup", "3",
+                           "--tokens", "4096")
     assert res.returncode == 0, res.stderr[-2000:]
     d = json.loads(lines[0])
     assert d["config"]["hidden"] == 1536 and d["config"]["intermediate"] == 4096

@@ -20,7 +20,7 @@ def test_cpp_host_known_answers():
     res = subprocess.run([exe], capture_output=True, text=True, timeout=120)
     print(res.stdout)
     assert res.returncode == 0, res.stdout + res.stderr
-    assert "all 13 tests passed" in res.stdout
+    assert "all 13 tests passed" in res.stdout and "ok   test_bf16_from_f32" in res.stdout
 
 
 def test_bounded_mbarrier_wait_self_test():

@@ -97,6 +97,16 @@ def test_rope_offset_equals_sliced_sequence(oracle, rng):
         assert np.array_equal(one_q[:, :, 0], full_q[:, :, p])
 
 
+def test_rope_token_major_is_the_transposed_head_major(oracle, rng):
+    """[B, S, H, D] rows rotate exactly as the same rows laid out [B, H, S, D]."""
+    q = rng.integers(0, 1 << 16, (2, 40, 3, 64), dtype=np.uint16) & 0xBFFF  # finite values
+    k = rng.integers(0, 1 << 16, (2, 40, 3, 64), dtype=np.uint16) & 0xBFFF
+    for table in (None, oracle.rope_table(77, 64, 10000.0)):
+        tq, tk = oracle.rope_embed_token_major(q, k, 37, 10000.0, table)
+        hq, hk = oracle.rope_embed(q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), 37, 10000.0, table)
+        assert np.array_equal(tq, hq.transpose(0, 2, 1, 3)) and np.array_equal(tk, hk.transpose(0, 2, 1, 3))
+
+
 def test_rope_preserves_pair_norm(oracle, rng):
     q, k = normal_bf16(rng, (1, 4, 256, 128)), normal_bf16(rng, (1, 4, 256, 128))
     q2, _ = oracle.rope_embed(q, k, offset=3000)

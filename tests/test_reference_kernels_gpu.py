@@ -1,8 +1,11 @@
 """GPU: this library against the reference's own kernels, run side by side.
 
-The reference kernels are compiled from the reference's sources
-(oracle/_ref/libref_kernels.so) and launched with its wrappers' launch
-configurations, on the same inputs as this library's kernels.  Where the
+The reference kernels are compiled from the reference's sources and launched
+with its wrappers' launch configurations, on the same inputs as this library's
+kernels, in two builds: sm_100a code (oracle/_ref/libref_kernels.so) and the
+form the reference ships, compute_80 PTX that the driver compiles when the
+library loads (oracle/_ref/libref_kernels_ptx.so, build.rs).  Every parity
+test runs against both.  Where the
 arithmetic is the same instruction for instruction -- residual add, SwiGLU
 (same __expf expression), embedding gather, RMSNorm (same reduction order),
 RoPE (same angle expression, fed through the in-kernel path or the table) --
@@ -19,17 +22,28 @@ import torch
 
 import hrm_layer_ops as ops
 from helpers import ULP_TOL, assert_bits_equal, normal_bf16, rope_pair_magnitude, to_dev, to_host
-from oracle import RefKernels, ulp_error
+from oracle import REF_LIB, REF_LIB_PTX, RefKernels, ulp_error
 
 pytestmark = pytest.mark.gpu
 
+REF_BUILDS = {"sm100a": REF_LIB, "ptx_compute80": REF_LIB_PTX}
+
+
+def _ref_kernels(path):
+    if not RefKernels.available(path):
+        pytest.skip(f"{os.path.basename(path)} is built only where the reference checkout exists "
+                    "(make -C oracle ref) and shipped prebuilt from there")
+    return RefKernels(path)
+
+
+@pytest.fixture(scope="module", params=sorted(REF_BUILDS))
+def ref(request):
+    return _ref_kernels(REF_BUILDS[request.param])
+
 
 @pytest.fixture(scope="module")
-def ref():
-    if not RefKernels.available():
-        pytest.skip("oracle/_ref/libref_kernels.so is built only where the reference checkout exists "
-                    "(make -C oracle ref) and shipped prebuilt from there")
-    return RefKernels()
+def ref_sm100a():
+    return _ref_kernels(REF_LIB)
 
 
 def test_additive_inject_matches_reference(ref, oracle, rng, cuda):
@@ -157,12 +171,14 @@ def _time_graph(calls, replays=50):
     return ms / len(calls)
 
 
-def test_throughput_vs_reference_kernels(ref, cuda):
+def test_throughput_vs_reference_kernels(ref_sm100a, cuda):
     """Both implementations at the full layer-op configurations, same inputs, same
     GPU, CUDA events (inputs > L2 except the 67 MB norm, which rotates 8 copies).
     Prints a JSON line (GB/s of algorithmic bytes) and requires this library to be
     at least as fast as the reference kernels on every op."""
     import json
+
+    ref = ref_sm100a
 
     g = torch.Generator(device=cuda).manual_seed(0)
     bf = torch.bfloat16

@@ -63,3 +63,15 @@ def test_device_equals_host(cuda):
     assert np.array_equal(got.view(torch.int16).cpu().numpy().view(np.uint16), want)
     ids = synth.ids(n, 3, synth.tag_of("ids"), 32000, start, device=cuda).cpu().numpy().astype(np.uint32)
     assert np.array_equal(ids, synth.ids_np(3, synth.tag_of("ids"), start, n, 32000))
+
+
+def test_oracle_generator_equals_numpy(oracle):
+    """The oracle's C generator (the CPU reference arm's inputs) gives the same
+    bits as the numpy path, so both arms of the benchmark see the same values."""
+    n = 1 << 20
+    for tag, start, std, mean in ((synth.tag_of("gate"), 12345, 0.5, 0.0),
+                                  (synth.tag_of("norm1_weight"), 0, 0.1, 1.0), (7, 1 << 40, 1.0, 0.0)):
+        got = oracle.fill_normal_bf16(np.empty(n, np.uint16), 0, tag, start, std, mean)
+        assert np.array_equal(got, synth.normal_bf16_np(0, tag, start, n, std, mean))
+    got = oracle.fill_ids(np.empty(n, np.uint32), 3, synth.tag_of("ids"), 32000, 999)
+    assert np.array_equal(got, synth.ids_np(3, synth.tag_of("ids"), 999, n, 32000))
