@@ -80,7 +80,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="chain",
                     choices=["chain", "add_rms_norm", "rms_norm_f32", "rms_norm", "rope", "swiglu", "embedding",
-                             "split_rope", "attn_gate", "convert_f32", "module"])
+                             "split_rope", "attn_gate", "convert_f32", "module", "load_checkpoint"])
     ap.add_argument("--tokens", type=int, default=CHAIN_B * CHAIN_S,
                     help="chain tokens per GPU (a multiple of 4096; default 65536)")
     ap.add_argument("--qk-layout", choices=["token", "head"], default="token",
@@ -88,6 +88,8 @@ def parse_args():
     ap.add_argument("--chunk-tokens", type=int, default=4096, help="e2e pipeline chunk (token-major Q/K)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-oracle baseline leg")
+    ap.add_argument("--ckpt", default=None, help="load_checkpoint: an existing safetensors file of the "
+                    "reference model's shapes (default: a synthetic one written for the run)")
     ap.add_argument("--dims", choices=sorted(DIMS), default="bench",
                     help="chain / module shapes: the benchmark's (default) or the reference's default model")
     args = ap.parse_args()
@@ -569,6 +571,169 @@ class SingleOp:
         return None
 
 
+class LoadCheckpoint:
+    """Checkpoint file -> bf16 device tensors at the reference model's shapes
+    (HrmConfig defaults, src/lib.rs:40-60: 16 layers per module, hidden 1536,
+    intermediate 4096, vocab 65536; 1.18 B parameters).  A synthetic
+    safetensors file is written once (f32 tensors, values ~ 0.02 N(0, 1)).
+
+    value: the GPU conversion of the file's raw bytes already in HBM into the
+    model's bf16 tensors (gate_up split), one launch per tensor piece, the
+    step's launches replayed from a CUDA graph; bytes = raw read + bf16
+    written.  e2e: the same bytes over the wall time of
+    hrm_layer_ops.checkpoint.load_safetensors on the file (page-cached reads
+    into pinned buffers, H2D, conversion on the GPU), plus a read-back of
+    z_L_init; file_gbs is the file's bytes over that time."""
+
+    name = "load_checkpoint"
+    LAYERS, H, I, V = 16, 1536, 4096, 65536
+
+    def __init__(self, device, rank, path=None, dtype="F32"):
+        import tempfile
+
+        import numpy as np
+        import torch
+
+        from hrm_layer_ops import checkpoint as ck
+        import hrm_layer_ops as ops
+
+        self.torch, self.ck, self.ops, self.device = torch, ck, ops, device
+        self.own_dir = None
+        if path is None:
+            base = "/dev/shm" if os.path.isdir("/dev/shm") else None
+            self.own_dir = tempfile.mkdtemp(prefix="hrm_ckpt_", dir=base)
+            path = os.path.join(self.own_dir, "model.safetensors")
+            self._write(path, dtype, np)
+        self.path = path
+        self.hdr = ck.read_header(path)
+        hdr = self.hdr
+        # the raw data section resident in HBM, and the destination tensors
+        size = os.path.getsize(path)
+        raw = np.fromfile(path, dtype=np.uint8, offset=hdr.data_offset, count=size - hdr.data_offset)
+        self.raw = torch.from_numpy(raw).to(device)
+        del raw
+        split = self.I * self.H
+        self.pieces = []  # (byte offset in the data section, numel, dtype name, destination)
+        for t in hdr.tensors:
+            es = ck.DTYPE_SIZES[t.dtype]
+            if t.name.endswith("gate_up_proj.weight"):  # split as src/lib.rs:2072-2078
+                parts = [(t.begin, split), (t.begin + split * es, t.numel - split)]
+            else:
+                parts = [(t.begin, t.numel)]
+            for b0, n in parts:
+                self.pieces.append((b0, n, t.dtype.lower(), torch.empty(n, dtype=torch.bfloat16, device=device)))
+        self.bytes_per_step = sum(n * (ck.DTYPE_SIZES[d.upper()] + 2) for _, n, d, _ in self.pieces)
+        self.rows_per_step = sum(n for _, n, _, _ in self.pieces)
+        self.file_bytes = size
+        self.kernels = ["convert_to_bf16"]
+        self.dominant = "convert_to_bf16"
+        self.kernel_bytes = {"convert_to_bf16": self.bytes_per_step}
+        self.footprint = self.bytes_per_step
+        self.config = {"workload": "checkpoint file -> bf16 device tensors, HRM-Text-1B shapes "
+                                   f"({self.LAYERS} layers x 2 modules, hidden {self.H}, intermediate {self.I}, "
+                                   f"vocab {self.V})", "dtype_in_file": dtype, "file_bytes": size,
+                       "tensor_pieces": len(self.pieces),
+                       "l2": f"{self.bytes_per_step / 1e9:.1f} GB moved per step vs 126 MB L2; no flush",
+                       "launch": "the step's conversions captured in a CUDA graph, replayed between the events"}
+        self.data = "synthetic safetensors file (f32, 0.02 N(0,1) tiled), written once per run"
+
+    def _write(self, path, dtype, np):
+        import json
+
+        es = {"F32": 4, "BF16": 2, "F16": 2}[dtype]
+        L, H, I, V = self.LAYERS, self.H, self.I, self.V
+        shapes = []
+        for mod in ("H", "L"):
+            for i in range(L):
+                p = f"model.{mod}_module.layers.{i}"
+                shapes += [(f"{p}.attn.gqkv_proj.weight", (4 * H, H)), (f"{p}.attn.o_proj.weight", (H, H)),
+                           (f"{p}.mlp.gate_up_proj.weight", (2 * I, H)), (f"{p}.mlp.down_proj.weight", (H, I))]
+        shapes += [("model.embed_tokens.weight", (V, H)), ("lm_head.weight", (V, H)), ("model.z_L_init", (H,))]
+        header, off = {}, 0
+        for name, shape in shapes:
+            n = int(np.prod(shape)) * es
+            header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [off, off + n]}
+            off += n
+        text = json.dumps(header).encode()
+        text += b" " * (-len(text) % 8)
+        block = (np.random.default_rng(0).standard_normal(1 << 22) * 0.02).astype(
+            {"F32": np.float32, "F16": np.float16, "BF16": np.float32}[dtype])
+        if dtype == "BF16":
+            block = (block.view(np.uint32) >> 16).astype(np.uint16)
+        block = block.tobytes()
+        with open(path, "wb") as f:
+            f.write(len(text).to_bytes(8, "little"))
+            f.write(text)
+            left = off
+            while left > 0:
+                k = min(left, len(block))
+                f.write(block[:k])
+                left -= k
+
+    def cpu_sample(self, min_seconds=5.0, sample_bytes=512 << 20):
+        """The reference's host conversion (raw_to_bf16, restated by the oracle,
+        all host threads) over the first 512 MB of the file's data section."""
+        import numpy as np
+
+        sys.path.insert(0, ROOT)
+        from oracle import Oracle
+
+        o = Oracle()
+        o.set_threads(len(os.sched_getaffinity(0)))
+        d = self.hdr.tensors[0].dtype
+        es = self.ck.DTYPE_SIZES[d]
+        n = sample_bytes // es
+        raw = np.fromfile(self.path, dtype=np.uint8, offset=self.hdr.data_offset, count=n * es).tobytes()
+        o.convert_to_bf16(raw, d.lower())
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            o.convert_to_bf16(raw, d.lower())
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= min_seconds:
+                break
+        sec = el / reps
+        return {"gbs": n * (es + 2) / sec / 1e9, "cores": o.max_threads(),
+                "sample": f"raw_to_bf16 of {n * es >> 20} MB of the file's {d} data on the host, {reps} reps, "
+                          f"oracle with {o.max_threads()} OpenMP threads"}
+
+    def close(self):
+        import shutil
+
+        if self.own_dir is not None:
+            shutil.rmtree(self.own_dir, ignore_errors=True)
+
+    def step(self, stream=None, events=None):
+        if events is not None:
+            events[0].record(stream)
+        for b0, n, d, out in self.pieces:
+            es = self.ck.DTYPE_SIZES[d.upper()]
+            self.ops.convert_to_bf16(self.raw[b0:b0 + n * es], d, out=out, stream=stream)
+        if events is not None:
+            events[1].record(stream)
+        return len(self.pieces)
+
+    def e2e(self, steps):
+        """Per step: the whole file -> device tensors through the public loader,
+        then z_L_init read back.  Host wall time (file reads are host work)."""
+        torch = self.torch
+        ms = []
+        w = None
+        for it in range(steps + 1):  # iteration 0 is the warm-up
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            w = self.ck.load_safetensors(self.path, self.LAYERS, self.H, self.I, device=self.device)
+            z = w.z_l_init.cpu()
+            t1 = time.perf_counter()
+            if it:
+                ms.append((t1 - t0) * 1e3)
+            del w
+        mean = sum(ms) / len(ms)
+        self.file_gbs = self.file_bytes / (mean / 1e3) / 1e9
+        h2d = self.file_bytes - self.hdr.data_offset
+        return mean, h2d, int(z.numel() * 2), steps * len(self.pieces)
+
+
 class Module:
     """One pass of a 4-layer H/L module over 16384 tokens: the layer loop's
     residual / norm / SwiGLU schedule (hrm_layer_ops.module.transformer_module:
@@ -728,6 +893,8 @@ def run_ours(args, world, rank, device, peers):
         wl = Chain(device, rank, world, args.tokens, args.qk_layout == "token", args.chunk_tokens)
     elif args.workload == "module":
         wl = Module(device, rank)
+    elif args.workload == "load_checkpoint":
+        wl = LoadCheckpoint(device, rank, args.ckpt)
     else:
         wl = SingleOp(args.workload, device, rank)
     stream = torch.cuda.current_stream(device)
@@ -745,7 +912,7 @@ def run_ours(args, world, rank, device, peers):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches = 0
     graph = None
-    if isinstance(wl, SingleOp):
+    if isinstance(wl, (SingleOp, LoadCheckpoint)):
         cap = torch.cuda.Stream(device)
         cap.wait_stream(stream)
         graph = torch.cuda.CUDAGraph()
@@ -800,10 +967,14 @@ def run_ours(args, world, rank, device, peers):
         e2e = {"value": round(world * wl.bytes_per_step / (ms_e2e / 1e3) / 1e9, 3), "unit": "GB/s",
                "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "path": ("pinned host buffers, H2D / kernels / D2H overlapped in chunks (public API)"
-                        if isinstance(wl, Chain) else "pinned host buffers, H2D -> kernels -> D2H on one stream "
-                                                      "(public API)")}
+                        if isinstance(wl, Chain) else
+                        "file (page cache) -> pinned ring -> H2D -> GPU conversion, hrm_layer_ops.checkpoint "
+                        "(public API), host wall time" if isinstance(wl, LoadCheckpoint) else
+                        "pinned host buffers, H2D -> kernels -> D2H on one stream (public API)")}
+        if isinstance(wl, LoadCheckpoint):
+            e2e["file_gbs"] = round(wl.file_gbs, 3)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu and isinstance(wl, Chain):
+    if rank == 0 and world == 1 and not args.no_cpu and isinstance(wl, (Chain, LoadCheckpoint)):
         c = wl.cpu_sample()
         cpu = {"value": round(c["gbs"], 3), "unit": "GB/s", "cores": c["cores"], "kind": "port",
                "sample": c["sample"]}
@@ -813,6 +984,8 @@ def run_ours(args, world, rank, device, peers):
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
+        if isinstance(wl, LoadCheckpoint):
+            wl.close()
         return
 
     peak, peak_kind = load_peaks()
@@ -843,6 +1016,8 @@ def run_ours(args, world, rank, device, peers):
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+    if isinstance(wl, LoadCheckpoint):
+        wl.close()
 
 
 if __name__ == "__main__":

@@ -296,6 +296,35 @@ int hrm_convert_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, hr
   return cuda_status(hrm::launch_convert_to_bf16(src, src_dtype, dst, n, as_cuda(stream)));
 }
 
+int hrm_upload_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, void* staging,
+                       int64_t staging_bytes, hrm_stream_t stream) {
+  if (src_dtype != HRM_DTYPE_BF16 && src_dtype != HRM_DTYPE_F32 && src_dtype != HRM_DTYPE_F16) return HRM_ERR_DTYPE;
+  if (n < 0 || staging_bytes < 0) return HRM_ERR_INVALID_SHAPE;
+  if (n == 0) return HRM_OK;
+  if (!src || !dst || !staging) return HRM_ERR_NULL_POINTER;
+  if (staging_bytes < 16) return HRM_ERR_INVALID_SHAPE;
+  const int64_t size = src_dtype == HRM_DTYPE_F32 ? 4 : 2;
+  const int64_t in_bytes = mul_checked(n, size), out_bytes = mul_checked(n, 2);
+  if (in_bytes < 0 || out_bytes < 0) return HRM_ERR_SIZE_OVERFLOW;
+  if (overlap(staging, staging_bytes, dst, out_bytes) || overlap(src, in_bytes, dst, out_bytes) ||
+      overlap(src, in_bytes, staging, staging_bytes))
+    return HRM_ERR_ALIASING;
+  const cudaStream_t s = as_cuda(stream);
+  // bf16 needs no conversion: one copy straight into dst.
+  if (src_dtype == HRM_DTYPE_BF16) return cuda_status(cudaMemcpyAsync(dst, src, (size_t)in_bytes, cudaMemcpyDefault, s));
+  // Pieces of a whole number of 16-byte groups, so that every piece starts the
+  // staging buffer with a whole element and its output at a whole element.
+  const int64_t piece = staging_bytes / 16 * 16;
+  for (int64_t off = 0; off < in_bytes; off += piece) {
+    const int64_t len = in_bytes - off < piece ? in_bytes - off : piece;
+    cudaError_t e = cudaMemcpyAsync(staging, static_cast<const char*>(src) + off, (size_t)len, cudaMemcpyDefault, s);
+    if (e != cudaSuccess) return cuda_status(e);
+    e = hrm::launch_convert_to_bf16(staging, src_dtype, static_cast<char*>(dst) + off / size * 2, len / size, s);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return HRM_OK;
+}
+
 int hrm_wait_timeouts(unsigned int* count, int reset) {
   if (!count) return HRM_ERR_NULL_POINTER;
   return cuda_status(hrm::rownorm_wait_timeouts(count, reset != 0));

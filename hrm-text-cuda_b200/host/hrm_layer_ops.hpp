@@ -31,10 +31,11 @@ struct bf16 {
 };
 
 // Mirrors HrmError (src/lib.rs:5-19): Driver = a CUDA error, InvalidInput =
-// a rejected argument, KernelNotFound = the kernel library is not usable.
+// a rejected argument, KernelNotFound = the kernel library is not usable,
+// Io = a checkpoint that cannot be read or deserialised.
 class HrmError : public std::runtime_error {
  public:
-  enum class Kind { Driver, InvalidInput, KernelNotFound };
+  enum class Kind { Driver, InvalidInput, KernelNotFound, Io };
   HrmError(Kind kind, int status, const std::string& what)
       : std::runtime_error(what), kind_(kind), status_(status) {}
   Kind kind() const { return kind_; }
@@ -132,6 +133,36 @@ class HrmLayerOps {
   // The same conversion into a new device slice, for a loader that keeps the
   // weights on the GPU (the reference converts on the host, then htod_copy).
   CudaSlice<bf16> htod_raw_as_bf16(int dtype, const uint8_t* raw, size_t nbytes) const;
+
+  // ---- checkpoint loading (src/lib.rs:2023-2125)
+  struct LayerWeights {  // src/lib.rs:62-69
+    CudaSlice<bf16> gqkv_proj, o_proj, gate_proj, up_proj, down_proj;
+  };
+  struct ModuleWeights {  // src/lib.rs:72-74
+    std::vector<LayerWeights> layers;
+  };
+  struct ModelWeights {  // src/lib.rs:77-83
+    ModuleWeights h_module, l_module;
+    CudaSlice<bf16> embed_tokens, lm_head, z_l_init;
+  };
+  // load_safetensors: the model's tensors from one safetensors file, as bf16
+  // device slices, with the reference's names and rules: per module
+  // ("model.H_module.layers", "model.L_module.layers") and layer, gqkv_proj,
+  // o_proj, gate_up_proj split at intermediate x hidden elements into
+  // gate_proj and up_proj, and down_proj, under ".attn." / ".mlp." when
+  // "model.H_module.layers.0.attn.gqkv_proj.weight" exists; then
+  // model.embed_tokens.weight, lm_head.weight (else model.lm_head.weight) and
+  // model.z_L_init.  The header is parsed and validated as safetensors 0.4.5
+  // does (safetensors.hpp); the bytes of the tensors used are read from the
+  // file in chunks into pinned host buffers (several reader threads), copied
+  // to the GPU and converted there (hrm_upload_to_bf16), reading chunk i + 1
+  // while chunk i is copied.  Returns once the weights are on the device.
+  // Throws HrmError Io for an unreadable or invalid file, InvalidInput for a
+  // missing tensor, a gate_up smaller than its gate half, or any tensor of a
+  // dtype other than BF16 / F32 / F16 (the reference converts every tensor
+  // of the file and panics on those).
+  ModelWeights load_safetensors(const std::string& path, size_t chunk_bytes = 64u << 20,
+                                int reader_threads = 4) const;
 
   // ---- fused entry points that replace wrapper sequences of the reference
   // additive_inject -> rms_norm (src/lib.rs:976-979); weight may be null.

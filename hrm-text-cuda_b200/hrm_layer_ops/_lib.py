@@ -45,6 +45,7 @@ SIGNATURES = {
     "hrm_gated_attn_output": [_p, _p, _p, _i64, _p],
     "hrm_broadcast_vec": [_p, _p, _i64, _i64, _p],
     "hrm_convert_to_bf16": [_p, ctypes.c_int, _p, _i64, _p],
+    "hrm_upload_to_bf16": [_p, ctypes.c_int, _p, _i64, _p, _i64, _p],
     "hrm_wait_timeouts": [ctypes.POINTER(ctypes.c_uint), ctypes.c_int],
     "hrm_abi_version": [],
 }

@@ -213,6 +213,23 @@ enum hrm_dtype { HRM_DTYPE_BF16 = 0, HRM_DTYPE_F32 = 1, HRM_DTYPE_F16 = 2 };
  * GPU.  dst must not overlap src.                                           */
 int hrm_convert_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, hrm_stream_t stream);
 
+/* Upload + conversion of one checkpoint tensor: n little-endian values of
+ * src_dtype at `src` -- host memory (pinned for full PCIe speed; pageable
+ * works, the copy then returns once the driver has staged the bytes) or
+ * device memory -- are copied, in pieces of at most staging_bytes, into the
+ * caller's device buffer `staging` and converted from there into the bf16
+ * device tensor `dst` with the rules of hrm_convert_to_bf16, all on
+ * `stream` (bf16 values need no conversion and are copied straight into
+ * dst).  Replaces the reference loader's raw_to_bf16 host loop followed
+ * by htod_copy (src/lib.rs:1981-2008, 2055-2112); its gate_up split
+ * (src/lib.rs:2072-2078) is two calls on the two halves of the tensor's
+ * bytes.  `staging` is scratch: the pieces reuse it in stream order, so no
+ * work on another stream may use it until `stream` has passed this call.
+ * staging_bytes >= 16 (a 16-byte aligned staging buffer takes the vectorised
+ * conversion); dst must not overlap staging or src.                         */
+int hrm_upload_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, void* staging,
+                       int64_t staging_bytes, hrm_stream_t stream);
+
 /* Number of bounded device-side waits that ran out on the current device
  * since the library was loaded there (or since the last reset).  The
  * bulk-copy kernels of the opt-in build wait on mbarriers with a deadline of

@@ -8,11 +8,14 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <fstream>
+#include <iterator>
 #include <functional>
 #include <string>
 #include <vector>
 
 #include "hrm_layer_ops.hpp"
+#include "safetensors.hpp"
 
 using hrm::bf16;
 using hrm::CudaSlice;
@@ -48,6 +51,140 @@ void test_bf16_from_f32() {
     std::memcpy(&f, &in[i], 4);
     expect(bf16::from_f32(f).bits == want[i], "from_f32 case " + std::to_string(i));
   }
+}
+
+std::string g_golden = "tests/golden";  // --golden DIR
+
+std::vector<uint8_t> file_bytes(const std::string& path) {
+  std::ifstream f(path, std::ios::binary);
+  expect((bool)f, "cannot open " + path);
+  return std::vector<uint8_t>(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
+}
+
+// The fixture checkpoints (tests/golden/make_checkpoint.py): header parsed in
+// data order, metadata read, the first tensor at the start of the data.
+void test_safetensors_header() {
+  const std::string path = g_golden + "/ckpt_tiny_attn.safetensors";
+  const auto h = hrm::SafetensorsHeader::read(path);
+  const auto bytes = file_bytes(path);
+  expect(h.tensors.size() == 21, "21 tensors");
+  expect(h.metadata.size() == 2 && h.metadata.at("format") == "pt", "metadata");
+  expect(h.tensors[0].name == "model.extra.odd_bias" && h.tensors[0].dtype == hrm::StDtype::BF16 &&
+             h.tensors[0].begin == 0 && h.tensors[0].end == 6,
+         "first tensor");
+  for (size_t i = 1; i < h.tensors.size(); ++i) expect(h.tensors[i].begin == h.tensors[i - 1].end, "data order");
+  expect(h.data_offset() % 8 == 0 && h.data_offset() + h.data_len() == bytes.size(), "data section");
+  const auto* g = h.find("model.L_module.layers.1.mlp.gate_up_proj.weight");
+  expect(g && g->shape.size() == 2 && g->shape[0] == 96 && g->shape[1] == 32, "gate_up shape");
+  // the same bytes through parse()
+  const auto h2 = hrm::SafetensorsHeader::parse(bytes.data(), bytes.size(), bytes.size());
+  expect(h2.tensors.size() == 21 && h2.header_len == h.header_len, "parse == read");
+  const auto f = hrm::SafetensorsHeader::read(g_golden + "/ckpt_tiny_flat.safetensors");
+  expect(f.tensors.size() == 19 && f.metadata.empty(), "flat file");
+}
+
+// exact f16 -> f32 widening (half's f16::to_f32), for the expected values
+float f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const int e = (h >> 10) & 0x1f;
+  const uint32_t m = h & 0x3ffu;
+  uint32_t bits;
+  if (e == 0x1f) {
+    bits = sign | (m ? 0x7fc00000u | (m << 13) : 0x7f800000u);
+  } else {
+    const float mag = e == 0 ? std::ldexp((float)m, -24) : std::ldexp((float)(m | 0x400u), e - 25);
+    std::memcpy(&bits, &mag, 4);
+    bits |= sign;
+  }
+  float out;
+  std::memcpy(&out, &bits, 4);
+  return out;
+}
+
+// The expected bf16 bits of elements [first, first + n) of tensor t: the
+// reference's raw_to_bf16 on the host (bf16 copied, f32 and f16 through
+// half's from_f32).
+std::vector<uint16_t> expected_bf16(const std::vector<uint8_t>& file, const hrm::SafetensorsHeader& h,
+                                    const hrm::StTensor& t, uint64_t first, uint64_t n) {
+  std::vector<uint16_t> out;
+  const size_t es = hrm::st_dtype_size(t.dtype);
+  const uint8_t* p = file.data() + h.data_offset() + t.begin + first * es;
+  for (uint64_t i = 0; i < n; ++i, p += es) {
+    if (t.dtype == hrm::StDtype::BF16) {
+      out.push_back((uint16_t)(p[0] | p[1] << 8));
+    } else if (t.dtype == hrm::StDtype::F16) {
+      out.push_back(bf16::from_f32(f16_to_f32((uint16_t)(p[0] | p[1] << 8))).bits);
+    } else {
+      const uint32_t u = (uint32_t)p[0] | (uint32_t)p[1] << 8 | (uint32_t)p[2] << 16 | (uint32_t)p[3] << 24;
+      float f;
+      std::memcpy(&f, &u, 4);
+      out.push_back(bf16::from_f32(f).bits);
+    }
+  }
+  return out;
+}
+
+// load_safetensors (src/lib.rs:2023-2125) on both fixture checkpoints, with
+// chunks small enough that tensors straddle chunk ends: every slice equals
+// the host conversion of its bytes, gate_up split at intermediate x hidden.
+void test_load_safetensors(HrmLayerOps& hrm) {
+  const hrm::HrmConfig saved = hrm.config;
+  hrm.config.n_layers = 2;
+  hrm.config.hidden_size = 32;
+  hrm.config.intermediate_size = 48;
+  for (const char* file : {"ckpt_tiny_attn.safetensors", "ckpt_tiny_flat.safetensors"}) {
+    for (size_t chunk : {(size_t)4096, (size_t)(64u << 20)}) {
+      const std::string path = g_golden + "/" + file;
+      const auto bytes = file_bytes(path);
+      const auto h = hrm::SafetensorsHeader::read(path);
+      auto w = hrm.load_safetensors(path, chunk, 3);
+      const bool attn = std::string(file).find("attn") != std::string::npos;
+      auto check_slice = [&](CudaSlice<bf16>&& s, const std::string& name, uint64_t first, uint64_t n) {
+        const hrm::StTensor* t = h.find(name);
+        expect(t != nullptr, "fixture has " + name);
+        expect(s.len() == n, name + ": length");
+        const auto got = hrm.sync_reclaim(std::move(s));
+        const auto want = expected_bf16(bytes, h, *t, first, n);
+        for (uint64_t i = 0; i < n; ++i)
+          expect(got[i].bits == want[i], name + ": element " + std::to_string(first + i));
+      };
+      const uint64_t split = 48 * 32;
+      for (int mod = 0; mod < 2; ++mod) {
+        auto& m = mod == 0 ? w.h_module : w.l_module;
+        expect(m.layers.size() == 2, "two layers");
+        for (size_t i = 0; i < 2; ++i) {
+          const std::string p = std::string(mod == 0 ? "model.H_module.layers." : "model.L_module.layers.") +
+                                std::to_string(i);
+          const std::string a = attn ? ".attn" : "", mm = attn ? ".mlp" : "";
+          check_slice(std::move(m.layers[i].gqkv_proj), p + a + ".gqkv_proj.weight", 0, 128 * 32);
+          check_slice(std::move(m.layers[i].o_proj), p + a + ".o_proj.weight", 0, 32 * 32);
+          check_slice(std::move(m.layers[i].gate_proj), p + mm + ".gate_up_proj.weight", 0, split);
+          check_slice(std::move(m.layers[i].up_proj), p + mm + ".gate_up_proj.weight", split, 96 * 32 - split);
+          check_slice(std::move(m.layers[i].down_proj), p + mm + ".down_proj.weight", 0, 32 * 48);
+        }
+      }
+      check_slice(std::move(w.embed_tokens), "model.embed_tokens.weight", 0, 20 * 32);
+      check_slice(std::move(w.lm_head), attn ? "lm_head.weight" : "model.lm_head.weight", 0, 20 * 32);
+      check_slice(std::move(w.z_l_init), "model.z_L_init", 0, 32);
+    }
+  }
+  // a missing tensor is InvalidInput, an unreadable file Io
+  hrm.config.n_layers = 3;
+  bool missing = false, io = false;
+  try {
+    hrm.load_safetensors(g_golden + "/ckpt_tiny_flat.safetensors");
+  } catch (const HrmError& e) {
+    missing = e.kind() == HrmError::Kind::InvalidInput &&
+              std::string(e.what()).find("missing tensor: model.H_module.layers.2.gqkv_proj.weight") == 0;
+  }
+  try {
+    hrm.load_safetensors(g_golden + "/no_such_file.safetensors");
+  } catch (const HrmError& e) {
+    io = e.kind() == HrmError::Kind::Io;
+  }
+  hrm.config = saved;
+  expect(missing, "missing tensor reported");
+  expect(io, "unreadable file reported");
 }
 
 // src/lib.rs:2227-2243
@@ -482,9 +619,32 @@ void test_recurrent_forward(HrmLayerOps&) {
 
 }  // namespace
 
+// --parse FILE: prints "ok <tensors> <data offset>" or "error <kind>" for the
+// header of FILE (the CPU tests compare it with the Python parser).
+int parse_only(const char* path) {
+  static const char* kinds[] = {"HeaderTooSmall",   "HeaderTooLarge",    "InvalidHeaderLength",
+                                "InvalidHeader",    "InvalidHeaderStart", "InvalidHeaderDeserialization",
+                                "InvalidOffset",    "TensorInvalidInfo", "ValidationOverflow",
+                                "MetadataIncompleteBuffer", "Io"};
+  try {
+    const auto h = hrm::SafetensorsHeader::read(path);
+    std::printf("ok %zu %llu\n", h.tensors.size(), (unsigned long long)h.data_offset());
+  } catch (const hrm::SafetensorsError& e) {
+    std::printf("error %s\n", kinds[(int)e.kind()]);
+  }
+  return 0;
+}
+
 int main(int argc, char** argv) {
+  bool host_only = false;
+  for (int i = 1; i < argc; ++i) {
+    if (std::strcmp(argv[i], "--host-only") == 0) host_only = true;
+    else if (std::strcmp(argv[i], "--golden") == 0 && i + 1 < argc) g_golden = argv[++i];
+    else if (std::strcmp(argv[i], "--parse") == 0 && i + 1 < argc) return parse_only(argv[++i]);
+  }
   const std::vector<std::pair<const char*, std::function<void()>>> host_tests = {
       {"test_bf16_from_f32", test_bf16_from_f32},
+      {"test_safetensors_header", test_safetensors_header},
   };
   for (const auto& t : host_tests) {
     try {
@@ -492,10 +652,13 @@ int main(int argc, char** argv) {
     } catch (const Failure& f) {
       std::printf("FAIL %s: %s\n", t.first, f.what.c_str());
       return 1;
+    } catch (const std::exception& e) {
+      std::printf("FAIL %s: %s\n", t.first, e.what());
+      return 1;
     }
     std::printf("ok   %s\n", t.first);
   }
-  if (argc > 1 && std::strcmp(argv[1], "--host-only") == 0) {
+  if (host_only) {
     std::printf("all %zu host tests passed\n", host_tests.size());
     return 0;
   }
@@ -510,6 +673,7 @@ int main(int argc, char** argv) {
       {"test_raw_to_bf16", test_raw_to_bf16},
       {"test_transformer_module", test_transformer_module},
       {"test_recurrent_forward", test_recurrent_forward},
+      {"test_load_safetensors", test_load_safetensors},
   };
   try {
     HrmLayerOps hrm(0);

@@ -182,11 +182,14 @@ def test_front_end_refuses_tensors_on_two_devices():
         ops._launch("hrm_swiglu_ffn", (t0, t0), SimpleNamespace(device=torch.device("cuda", 1)))
 
 
-def test_cpp_host_conversions_without_a_gpu():
-    """The C++ host layer's own f32 -> bf16 (half's from_f32, NaN rule included)."""
+def test_cpp_host_code_without_a_gpu():
+    """The C++ host layer's own f32 -> bf16 (half's from_f32, NaN rule
+    included) and its safetensors header parser on the fixture checkpoints."""
     import subprocess
 
+    from conftest import GOLDEN
+
     exe = os.path.join(PKG, "build", "test_layer_ops")
-    res = subprocess.run([exe, "--host-only"], capture_output=True, text=True, timeout=60)
+    res = subprocess.run([exe, "--host-only", "--golden", GOLDEN], capture_output=True, text=True, timeout=60)
     assert res.returncode == 0, res.stdout + res.stderr
-    assert "all 1 host tests passed" in res.stdout
+    assert "all 2 host tests passed" in res.stdout

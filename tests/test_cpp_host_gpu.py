@@ -9,7 +9,7 @@ import subprocess
 
 import pytest
 
-from conftest import PKG
+from conftest import GOLDEN, PKG
 
 pytestmark = pytest.mark.gpu
 
@@ -17,10 +17,11 @@ pytestmark = pytest.mark.gpu
 def test_cpp_host_known_answers():
     exe = os.path.join(PKG, "build", "test_layer_ops")
     assert os.path.exists(exe), "build with make -C hrm-text-cuda_b200"
-    res = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    res = subprocess.run([exe, "--golden", GOLDEN], capture_output=True, text=True, timeout=120)
     print(res.stdout)
     assert res.returncode == 0, res.stdout + res.stderr
-    assert "all 13 tests passed" in res.stdout and "ok   test_bf16_from_f32" in res.stdout
+    assert "all 14 tests passed" in res.stdout and "ok   test_bf16_from_f32" in res.stdout
+    assert "ok   test_safetensors_header" in res.stdout and "ok   test_load_safetensors" in res.stdout
 
 
 def test_bounded_mbarrier_wait_self_test():
