@@ -426,132 +426,6 @@ __global__ void __launch_bounds__(32 * kBkMaxWarps, 1) rownorm_bulk_kernel(const
 
 #endif  // HRM_RN_BULK
 
-
-// ------------------------------------------- launch-resident path (RMSNorm)
-// For a launch whose rows fit, one CTA per SM, in the SM's shared memory: CTA
-// b takes the balanced row range [b R / G, (b + 1) R / G) of R rows over G
-// CTAs and, at its start, copies every one of those rows into shared memory
-// with the bulk-copy engine (cp.async.bulk, one mbarrier per row, no
-// multicast).  The whole launch's input is therefore in flight from the first
-// microsecond, instead of the one row per warp (a register-held row) that the
-// warp-per-row grid keeps in flight, which at 4096 rows of 2048 needs 1.2
-// (bf16) to 1.7 (fp32) waves of CTAs and ends in a partial wave.  Warp w then
-// normalises rows w, w + W, ... in arrival order: the row from shared memory
-// into registers (lane l holds 16-byte chunks l, l + 32, ...: the lane layout
-// of the warp-per-row kernels, so the same reduction replays the reference's
-// order bit for bit), the weight kept in registers, the outputs stored with
-// evict-first hints.  Waits are bounded (warp_wait_bounded).
-#ifndef HRM_RN_RESIDENT
-#define HRM_RN_RESIDENT 1
-#endif
-
-struct ResArgs {
-  const uint4* x;   // rows of 16-byte chunks (8 bf16 or 4 fp32 values each)
-  uint4* y;
-  const uint4* w;   // weight chunks, or null
-  int64_t rows;
-  int nchunks;      // 16-byte chunks per row
-  int hidden;       // elements per row
-  int max_rows;     // row slots per CTA (>= every CTA's row count)
-  float eps;
-};
-
-template <bool F32, int VPL, bool HAS_W, int THREADS>
-__global__ void __launch_bounds__(THREADS, 1) rownorm_resident_kernel(const ResArgs a) {
-  grid_dependency_begin();
-  extern __shared__ uint4 smem[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int kW = THREADS / 32;
-  const int64_t r0 = (int64_t)blockIdx.x * a.rows / gridDim.x;
-  const int n = (int)((int64_t)(blockIdx.x + 1) * a.rows / gridDim.x - r0);  // <= a.max_rows
-  const uint32_t row_bytes = (uint32_t)a.nchunks * 16u;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (int64_t)a.max_rows * a.nchunks);
-
-  // Lane 0 of warp w owns rows w, w + kW, ...: it initialises their barriers
-  // and issues all of their copies at once.
-  if (lane == 0) {
-    for (int i = warp; i < n; i += kW) mbar_init(smem_addr(&bars[i]), 1);
-    mbar_init_fence();
-    const uint64_t policy = l2_evict_first_policy();
-    for (int i = warp; i < n; i += kW) {
-      mbar_arrive_expect_tx(smem_addr(&bars[i]), row_bytes);
-      bulk_g2s_hint(smem_addr(smem + (int64_t)i * a.nchunks), a.x + (r0 + i) * a.nchunks, row_bytes,
-                    smem_addr(&bars[i]), policy);
-    }
-  }
-  __syncwarp();
-  uint4 wv[HAS_W ? VPL : 1];
-  if (HAS_W) {
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int c = lane + 32 * j;
-      if (c < a.nchunks) wv[j] = ld_keep(a.w + c);
-    }
-  }
-
-  for (int i = warp; i < n; i += kW) {
-    if (!warp_wait_bounded(smem_addr(&bars[i]), 0)) {
-      // Report, then wait (bounded) for this warp's copies that may still be
-      // in flight, so that none lands in shared memory after the CTA is gone.
-      if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
-      for (int k = i; k < n; k += kW) warp_wait_bounded(smem_addr(&bars[k]), 0);
-      return;
-    }
-    const uint4* src = smem + (int64_t)i * a.nchunks;
-    uint4* dst = a.y + (r0 + i) * a.nchunks;
-    uint4 v[VPL];
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int c = lane + 32 * j;
-      if (c < a.nchunks) v[j] = src[c];
-    }
-    if (F32) {
-      float pa[4] = {0.f, 0.f, 0.f, 0.f}, pc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int c = lane + 32 * j;
-        if (c < a.nchunks) {
-          float(&p)[4] = (j & 1) ? pc : pa;
-          const float4 f = *reinterpret_cast<const float4*>(&v[j]);
-          p[0] = fmaf(f.x, f.x, p[0]);
-          p[1] = fmaf(f.y, f.y, p[1]);
-          p[2] = fmaf(f.z, f.z, p[2]);
-          p[3] = fmaf(f.w, f.w, p[3]);
-        }
-      }
-      const float inv = inv_rms(ref_tree_f32(pa, pc), a.hidden, a.eps);
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int c = lane + 32 * j;
-        if (c < a.nchunks) {
-          const float4 f = *reinterpret_cast<const float4*>(&v[j]);
-          float4 o = make_float4(f.x * inv, f.y * inv, f.z * inv, f.w * inv);
-          if (HAS_W) {
-            const float4 ww = *reinterpret_cast<const float4*>(&wv[j]);
-            o.x = o.x * ww.x; o.y = o.y * ww.y; o.z = o.z * ww.z; o.w = o.w * ww.w;
-          }
-          __stcs(reinterpret_cast<float4*>(dst + c), o);
-        }
-      }
-    } else {
-      float p[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) p[e] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int c = lane + 32 * j;
-        if (c < a.nchunks) accum8(p, v[j]);
-      }
-      const float inv = inv_rms(ref_tree_bf16(p), a.hidden, a.eps);
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int c = lane + 32 * j;
-        if (c < a.nchunks) st_stream(dst + c, norm8<HAS_W>(v[j], inv, HAS_W ? wv[j] : make_uint4(0, 0, 0, 0)));
-      }
-    }
-  }
-}
-
 // ------------------------------------------------------------ fp32 fast path
 struct RowArgsF32 {
   const float4* x;
@@ -703,24 +577,6 @@ __global__ void __launch_bounds__(kBlockThreads) rownorm_block_kernel(const RowA
 }
 
 // ------------------------------------------------------------ dispatch
-#if HRM_RN_RESIDENT || HRM_RN_BULK
-// Opt-in dynamic shared memory per CTA of the current device, cached per device.
-int smem_optin_bytes() {
-  static std::atomic<int> cache[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  int v = (dev >= 0 && dev < 64) ? cache[dev].load(std::memory_order_relaxed) : 0;
-  if (v > 0) return v;
-  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0) {
-    cudaGetLastError();
-    v = 48 * 1024;
-  }
-  if (dev >= 0 && dev < 64) cache[dev].store(v, std::memory_order_relaxed);
-  return v;
-}
-#endif
-
-
 template <typename K>
 int resident_ctas(K kernel, size_t smem) {
   int n = 0;
@@ -763,6 +619,21 @@ cudaError_t dispatch_vpl(const RowArgs& a, cudaStream_t s) {
 }
 
 #if HRM_RN_BULK
+// Opt-in dynamic shared memory per CTA of the current device, cached per device.
+int smem_optin_bytes() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  int v = (dev >= 0 && dev < 64) ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (v > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0) {
+    cudaGetLastError();
+    v = 48 * 1024;
+  }
+  if (dev >= 0 && dev < 64) cache[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
 // Warps per CTA of the bulk path (as many stage rings as fit, at most
 // kBkMaxWarps) and the dynamic shared memory they need; 0 warps: no fit.
 int bulk_plan(int nchunks, int rows_per_stage, bool has_w, size_t* smem) {
@@ -818,64 +689,6 @@ cudaError_t dispatch_bulk(const RowArgs& a, int nwarps, size_t smem, cudaStream_
 }
 
 #endif  // HRM_RN_BULK
-
-
-#if HRM_RN_RESIDENT
-// Threads per CTA of the resident kernel: 16 warps where a lane's row and weight
-// chunks leave room for them (<= 128 registers), else 8.
-template <int VPL>
-constexpr int resident_threads() {
-  return VPL >= 16 ? 256 : 512;
-}
-
-template <bool F32, int VPL, bool HAS_W>
-cudaError_t launch_resident_on(const ResArgs& a, int grid, size_t smem, cudaStream_t s) {
-  constexpr int kT = resident_threads<VPL>();
-  auto kernel = rownorm_resident_kernel<F32, VPL, HAS_W, kT>;
-  static std::atomic<bool> opted[64];  // the opt-in is per function and device
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  if (dev < 0 || dev >= 64 || !opted[dev].load(std::memory_order_relaxed)) {
-    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin_bytes());
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) opted[dev].store(true, std::memory_order_relaxed);
-  }
-  return launch_kernel(kernel, grid, kT, smem, s, a);
-}
-
-// Launches the resident RMSNorm when the launch's rows fit one CTA per SM and
-// there are enough of them (at least 8 per SM: smaller launches keep the
-// warp-per-row grid, which spreads a few rows over many SMs); returns false
-// (nothing launched) otherwise.
-template <bool F32, bool HAS_W>
-bool try_resident(const void* x, void* y, const void* w, int64_t rows, int hidden, float eps, cudaStream_t s,
-                  cudaError_t* err) {
-  const int per_chunk = F32 ? 4 : 8;
-  const int nchunks = hidden / per_chunk;
-  const int need = (nchunks + 31) / 32;
-  const int64_t G = device_sm_count();
-  if (need > 16 || rows < 8 * G) return false;
-  const int64_t max_rows = (rows + G - 1) / G;
-  const size_t smem = (size_t)max_rows * ((size_t)nchunks * 16 + 8);
-  if (smem > (size_t)smem_optin_bytes()) return false;
-  ResArgs a;
-  a.x = static_cast<const uint4*>(x);
-  a.y = static_cast<uint4*>(y);
-  a.w = static_cast<const uint4*>(w);
-  a.rows = rows;
-  a.nchunks = nchunks;
-  a.hidden = hidden;
-  a.max_rows = (int)max_rows;
-  a.eps = eps;
-  const int grid = (int)G;
-  if (need <= 1) *err = launch_resident_on<F32, 1, HAS_W>(a, grid, smem, s);
-  else if (need <= 2) *err = launch_resident_on<F32, 2, HAS_W>(a, grid, smem, s);
-  else if (need <= 4) *err = launch_resident_on<F32, 4, HAS_W>(a, grid, smem, s);
-  else if (need <= 8) *err = launch_resident_on<F32, 8, HAS_W>(a, grid, smem, s);
-  else *err = launch_resident_on<F32, 16, HAS_W>(a, grid, smem, s);
-  return true;
-}
-#endif  // HRM_RN_RESIDENT
 
 template <typename T, int MODE, bool HAS_W>
 cudaError_t launch_block(const RowArgsScalar& a, cudaStream_t s) {
@@ -973,14 +786,6 @@ cudaError_t rownorm_wait_timeouts(unsigned int* count, bool reset) {
 
 cudaError_t launch_rms_norm_bf16(const void* x, void* y, const void* w, int64_t rows, int64_t hidden, float eps,
                                  cudaStream_t s) {
-#if HRM_RN_RESIDENT
-  if (hidden % 8 == 0 && hidden <= 4096 && aligned16(x) && aligned16(y) && (w == nullptr || aligned16(w))) {
-    cudaError_t err = cudaSuccess;
-    if (w ? try_resident<false, true>(x, y, w, rows, (int)hidden, eps, s, &err)
-          : try_resident<false, false>(x, y, w, rows, (int)hidden, eps, s, &err))
-      return err;
-  }
-#endif
   return launch_bf16_rows<kRms>(x, nullptr, nullptr, nullptr, y, w, rows, hidden, 0, 1.0f, eps, s);
 }
 
@@ -1000,12 +805,6 @@ cudaError_t launch_rms_norm_f32(const float* x, float* y, const float* w, int64_
   const bool fast = hidden % 4 == 0 && hidden / 4 <= kMaxVpl * 32 && aligned16(x) && aligned16(y) &&
                     (w == nullptr || aligned16(w));
   if (fast) {
-#if HRM_RN_RESIDENT
-    cudaError_t err = cudaSuccess;
-    if (w ? try_resident<true, true>(x, y, w, rows, (int)hidden, eps, s, &err)
-          : try_resident<true, false>(x, y, w, rows, (int)hidden, eps, s, &err))
-      return err;
-#endif
     RowArgsF32 a;
     a.x = reinterpret_cast<const float4*>(x);
     a.y = reinterpret_cast<float4*>(y);

@@ -89,8 +89,7 @@ def test_broadcast(cuda, copies, vec, shift):
     o.check("broadcast_vec")
 
 
-# ... plus launches of at least 8 rows per SM, which the launch-resident
-# RMSNorm takes (one CTA per SM, rows staged in shared memory).
+# ... plus launches of several waves of CTAs.
 ROW_SHAPES = [(1, 8), (3, 2048), (17, 1536), (5, 200), (2, 6144), (1, 4), (9, 8200), (64, 4096), (1184, 8),
               (1500, 200), (4096, 2048), (2000, 4096)]
 

@@ -38,7 +38,22 @@ def _ref_kernels(path):
 
 @pytest.fixture(scope="module", params=sorted(REF_BUILDS))
 def ref(request):
-    return _ref_kernels(REF_BUILDS[request.param])
+    k = _ref_kernels(REF_BUILDS[request.param])
+    k.build = request.param
+    return k
+
+
+def assert_rope_equal(ref, got, want, what):
+    """RoPE outputs vs the reference kernel: bit for bit against its sm_100a
+    build.  The form the reference ships (compute_80 PTX compiled by the driver
+    at load time) disagrees with that build in about 1e-5 of the outputs, by one
+    bf16 ulp (measured on a B200 with driver 580), so against it the bar is 1
+    ulp at the pair's magnitude with at least 99.99% of the elements identical."""
+    if ref.build == "sm100a":
+        assert_bits_equal(got, want, what)
+        return
+    err = ulp_error(got, want, rope_pair_magnitude(want))
+    assert err.max() <= 1.0 and np.mean(err == 0) >= 0.9999, (what, float(err.max()), float(np.mean(err == 0)))
 
 
 @pytest.fixture(scope="module")
@@ -105,8 +120,8 @@ def test_rope_matches_reference(ref, oracle, rng, cuda, b, h, s, d, off, use_tab
     ref.rope_embed(rq, rk, off, 10000.0)
     mq, mk = to_dev(q, cuda), to_dev(k, cuda)
     ops.rope_embed(mq, mk, off, 10000.0, ops.rope_table(off + s, d) if use_table else None)
-    assert_bits_equal(to_host(mq), to_host(rq), "q vs reference")
-    assert_bits_equal(to_host(mk), to_host(rk), "k vs reference")
+    assert_rope_equal(ref, to_host(mq), to_host(rq), "q vs reference")
+    assert_rope_equal(ref, to_host(mk), to_host(rk), "k vs reference")
     oq, ok = oracle.rope_embed(q, k, off, 10000.0)
     for got, want in ((oq, to_host(rq)), (ok, to_host(rk))):
         assert ulp_error(got, want, rope_pair_magnitude(want)).max() <= ULP_TOL
@@ -332,7 +347,10 @@ def test_split_gqkv_rope_matches_reference_sequence(ref, rng, cuda, b, s, h, d, 
     table = ops.rope_table(off + s, d) if use_table else None
     outs = ops.split_gqkv_rope(gqkv, h, off, 10000.0, table, mkc, mvc, cache_offset=off)
     for got, want, name in zip((*outs, mkc, mvc), (rg, rq, rk, rv, rkc, rvc), ("gate", "q", "k", "v", "kc", "vc")):
-        assert_bits_equal(to_host(got), to_host(want), name)
+        if name in ("q", "k", "kc"):
+            assert_rope_equal(ref, to_host(got), to_host(want), name)
+        else:
+            assert_bits_equal(to_host(got), to_host(want), name)
 
 
 @pytest.mark.parametrize("b,s,h,d", [(2, 256, 16, 128), (1, 77, 12, 64), (3, 5, 2, 128)])
@@ -351,7 +369,10 @@ def test_split_gqkv_rope_matches_reference_prefill_cache_form(ref, rng, cuda, b,
     mkc, mvc = kc0.clone(), vc0.clone()
     outs = ops.split_gqkv_rope(gqkv, h, 0, 10000.0, None, mkc, mvc, cache_offset=0)
     for got, want, name in zip((*outs, mkc, mvc), (rg, rq, rk, rv, rkc, rvc), ("gate", "q", "k", "v", "kc", "vc")):
-        assert_bits_equal(to_host(got), to_host(want), name)
+        if name in ("q", "k", "kc"):
+            assert_rope_equal(ref, to_host(got), to_host(want), name)
+        else:
+            assert_bits_equal(to_host(got), to_host(want), name)
 
 
 def test_attn_gate_and_broadcast_match_reference(ref, rng, cuda):
@@ -382,8 +403,8 @@ def test_rope_long_context_matches_reference(ref, oracle, rng, cuda, theta, off,
     ref.rope_embed(rq, rk, off, theta)
     mq, mk = to_dev(q, cuda), to_dev(k, cuda)
     ops.rope_embed(mq, mk, off, theta, ops.rope_table(off + s, d, theta) if use_table else None)
-    assert_bits_equal(to_host(mq), to_host(rq), "q vs reference")
-    assert_bits_equal(to_host(mk), to_host(rk), "k vs reference")
+    assert_rope_equal(ref, to_host(mq), to_host(rq), "q vs reference")
+    assert_rope_equal(ref, to_host(mk), to_host(rk), "k vs reference")
     oq, ok = oracle.rope_embed(q, k, off, theta)
     for got, want in ((to_host(mq), oq), (to_host(mk), ok)):
         assert ulp_error(got, want, rope_pair_magnitude(want)).max() <= ULP_TOL
