@@ -922,9 +922,14 @@ def run_ours(args, world, rank, device, peers):
         # One untimed replay first: the first launch of a new graph also uploads
         # it to the device (about 2 us per node here), which is not the steps' time.
         graph.replay()
-        # ... then flush L2 (a 256 MB write), so that the timed replay's first
-        # steps do not find the warm-up replay's last inputs there.
-        torch.empty(256 << 20, dtype=torch.uint8, device=device).zero_()
+        # ... then flush L2 by reading 256 MB (a read leaves only clean lines
+        # behind, so no write-back of the flush lands in the timed region), so
+        # that the timed replay's first steps do not find the warm-up replay's
+        # last inputs there.
+        flush = torch.ones(256 << 20, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize()
+        flush.sum()
+        del flush
         torch.cuda.synchronize()
         wl.config["launch"] = (f"CUDA graph of the {args.steps} timed steps, replayed once untimed (graph upload), "
                                "then once between the events")

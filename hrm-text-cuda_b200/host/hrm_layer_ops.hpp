@@ -162,7 +162,7 @@ class HrmLayerOps {
   // dtype other than BF16 / F32 / F16 (the reference converts every tensor
   // of the file and panics on those).
   ModelWeights load_safetensors(const std::string& path, size_t chunk_bytes = 64u << 20,
-                                int reader_threads = 4) const;
+                                int reader_threads = 8) const;
 
   // ---- fused entry points that replace wrapper sequences of the reference
   // additive_inject -> rms_norm (src/lib.rs:976-979); weight may be null.
