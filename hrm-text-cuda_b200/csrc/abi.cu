@@ -63,6 +63,7 @@ const char* hrm_status_string(int status) {
     case HRM_ERR_ALIASING: return "buffers that must be distinct overlap";
     case HRM_ERR_TABLE_RANGE: return "position_offset + seq_len exceeds the rope table";
     case HRM_ERR_DTYPE: return "unsupported dtype";
+    case HRM_ERR_SCRATCH_LIMIT: return "request exceeds the fixed device scratch of an allocation-free entry point";
     default: break;
   }
   if (status > HRM_ERR_CUDA) return cudaGetErrorString(static_cast<cudaError_t>(status - HRM_ERR_CUDA));

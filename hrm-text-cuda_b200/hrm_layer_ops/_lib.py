@@ -20,6 +20,8 @@ HRM_ERR_SIZE_OVERFLOW = 3
 HRM_ERR_ALIASING = 4
 HRM_ERR_TABLE_RANGE = 5
 HRM_ERR_DTYPE = 6
+HRM_ERR_SCRATCH_LIMIT = 7
+UPLOAD_STATIC_BYTES = 16 * 1024 * 1024  # HRM_UPLOAD_STATIC_BYTES
 DTYPES = {"bf16": 0, "f32": 1, "f16": 2}
 HRM_ERR_CUDA = 1000
 
@@ -46,6 +48,7 @@ SIGNATURES = {
     "hrm_broadcast_vec": [_p, _p, _i64, _i64, _p],
     "hrm_convert_to_bf16": [_p, ctypes.c_int, _p, _i64, _p],
     "hrm_upload_to_bf16": [_p, ctypes.c_int, _p, _i64, _p, _i64, _p],
+    "hrm_upload_to_bf16_static": [_p, ctypes.c_int, _p, _i64, _p],
     "hrm_wait_timeouts": [ctypes.POINTER(ctypes.c_uint), ctypes.c_int],
     "hrm_abi_version": [],
 }

@@ -41,6 +41,7 @@ enum hrm_status {
   HRM_ERR_ALIASING = 4,       /* buffers that must be distinct overlap           */
   HRM_ERR_TABLE_RANGE = 5,    /* position_offset + seq_len exceeds the rope table */
   HRM_ERR_DTYPE = 6,          /* unsupported element type                        */
+  HRM_ERR_SCRATCH_LIMIT = 7,  /* request larger than a fixed in-library scratch  */
   HRM_ERR_CUDA = 1000         /* HRM_ERR_CUDA + cudaError_t of the failed launch  */
 };
 
@@ -229,6 +230,29 @@ int hrm_convert_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, hr
  * conversion); dst must not overlap staging or src.                         */
 int hrm_upload_to_bf16(const void* src, int src_dtype, void* dst, int64_t n, void* staging,
                        int64_t staging_bytes, hrm_stream_t stream);
+
+/* Bytes of device scratch compiled into the library for
+ * hrm_upload_to_bf16_static (held on every GPU the library is loaded on). */
+#define HRM_UPLOAD_STATIC_BYTES (16 * 1024 * 1024)
+
+/* hrm_upload_to_bf16 without the caller's staging buffer, for callers that
+ * must not allocate device memory: a process whose GPU memory is reserved in
+ * full by another allocator (a serving engine's pool, a framework's caching
+ * allocator), or one that reloads weights while other streams run and cannot
+ * afford cudaMalloc's device synchronisation.  No counterpart in the
+ * reference.  The raw bytes go through a fixed device array of
+ * HRM_UPLOAD_STATIC_BYTES inside the library, which every GPU that loads the
+ * library holds until the process exits.  Limit: an f32 or f16 request of more
+ * than HRM_UPLOAD_STATIC_BYTES raw bytes returns HRM_ERR_SCRATCH_LIMIT (upload
+ * a larger tensor in several calls on consecutive element ranges; the
+ * conversion is elementwise); bf16 is copied straight into dst and has no
+ * limit.  The call allocates nothing (no cudaMalloc, no cudaFree).  The first
+ * call on a device looks up the array's address there (cudaGetSymbolAddress,
+ * with that device current); make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU (on different
+ * streams, or from several host threads) race on it, so order them on one
+ * stream.  Results equal hrm_upload_to_bf16's bit for bit.                  */
+int hrm_upload_to_bf16_static(const void* src, int src_dtype, void* dst, int64_t n, hrm_stream_t stream);
 
 /* Number of bounded device-side waits that ran out on the current device
  * since the library was loaded there (or since the last reset).  The
