@@ -6,12 +6,16 @@
 // registers, so the row is read from HBM exactly once (the reference reads it
 // twice, src/kernels/rms_norm.cu:28 and :62).  Lane l holds the 16-byte chunks
 // l, l+32, l+64, ... of its row, so every warp-wide access is one contiguous
-// 512-byte span.  A CTA of 8 warps (fewer for a launch with fewer than 8 rows
+// 512-byte span.  A CTA of 4 warps (fewer for a launch with fewer than 4 rows
 // per SM, so that small launches spread over more SMs) copies the optional
 // weight vector into shared memory with cp.async while its first rows load;
 // the grid has one warp per row (measured on B200: 6.7 TB/s for add + RMSNorm
 // vs 6.05 TB/s with a persistent one-wave grid), and the warps still loop if a
-// launch exceeds the grid limit.
+// launch exceeds the grid limit.  4-warp CTAs, against 8, refill an SM at a
+// finer grain when a launch ends in a partial wave: RMSNorm [4096 x 2048]
+// 7.22 -> 7.05 us (bf16) and 12.14 -> 11.91 us (fp32) in back-to-back
+// launches, add + RMSNorm [16384 x 2048] 6283 -> 6390 GB/s; 2 and 16 warps
+// were slower.
 //
 // Reduction order.  rms_norm_kernel runs 256 threads per row: thread t
 // accumulates x[t], x[t+256], ... with fused multiply-add (src/kernels/
@@ -38,29 +42,33 @@ namespace {
 // Launch shape of the warp-per-row kernels (compile-time; defaults tuned):
 //   HRM_RN_WARPS      warps per CTA
 //   HRM_RN_WAVES      grid cap in waves of resident CTAs (0: one warp per row)
-//   HRM_RN_MINBLOCKS  __launch_bounds__ minimum resident CTAs per SM (2: at most
-//                     128 registers, which keeps embed + RMSNorm at 3 CTAs per
-//                     SM and the fp32 kernel at 2 with no spills)
+//   HRM_RN_MAXREGS    register cap per thread (128: no spills, and 2048-wide
+//                     rows keep 16-24 warps per SM), enforced through the
+//                     __launch_bounds__ minimum of resident CTAs
 #ifndef HRM_RN_WARPS
-#define HRM_RN_WARPS 8
+#define HRM_RN_WARPS 4
 #endif
 #ifndef HRM_RN_WAVES
 #define HRM_RN_WAVES 0
 #endif
+#ifndef HRM_RN_MAXREGS
+#define HRM_RN_MAXREGS 128
+#endif
 // Grid cap of the fp32 kernel, in waves (0: one warp per row), and its
-// __launch_bounds__ minimum resident CTAs per SM.
+// register cap.
 #ifndef HRM_RN_F32_WAVES
 #define HRM_RN_F32_WAVES HRM_RN_WAVES
 #endif
-#ifndef HRM_RN_F32_MINBLOCKS
-#define HRM_RN_F32_MINBLOCKS HRM_RN_MINBLOCKS
-#endif
-#ifndef HRM_RN_MINBLOCKS
-#define HRM_RN_MINBLOCKS 2
+#ifndef HRM_RN_F32_MAXREGS
+#define HRM_RN_F32_MAXREGS HRM_RN_MAXREGS
 #endif
 
 constexpr int kWarps = HRM_RN_WARPS;          // warp-per-row kernels
 constexpr int kThreads = 32 * kWarps;
+// __launch_bounds__ minimum resident CTAs that caps a thread at max_regs.
+constexpr int min_blocks_for(int max_regs) {
+  return 65536 / (kThreads * max_regs) < 1 ? 1 : 65536 / (kThreads * max_regs);
+}
 constexpr int kBlockThreads = 256;            // reference-shaped fallback: 8 warps per row
 constexpr int kBlockWarps = kBlockThreads / 32;
 constexpr int kMaxVpl = 16;
@@ -191,15 +199,15 @@ __device__ __forceinline__ void publish_weight() {
   __syncthreads();
 }
 
-// Minimum resident CTAs: HRM_RN_MINBLOCKS (<= 128 registers per thread), except
+// Register cap: HRM_RN_MAXREGS, except
 // - add + RMSNorm over rows of more than 2048 elements, whose x and branch
 //   chunks (2 x 16 per lane) need more registers than that without spilling;
 // - plain and embed + RMSNorm over rows of at most 1536 elements (<= 6 chunks
-//   per lane), which fit 4 CTAs (64 registers): embed + RMSNorm at the
-//   reference model's hidden 1536 measured 6.36 -> 6.46 TB/s with it.
+//   per lane), capped at 64 registers for more warps per SM: embed + RMSNorm
+//   at the reference model's hidden 1536 measured 6.36 -> 6.46 TB/s with it.
 template <int VPL, int MODE>
 constexpr int rownorm_min_blocks() {
-  return (MODE == kAdd && VPL > 8) ? 1 : ((MODE != kAdd && VPL <= 6) ? 4 : HRM_RN_MINBLOCKS);
+  return min_blocks_for((MODE == kAdd && VPL > 8) ? 255 : ((MODE != kAdd && VPL <= 6) ? 64 : HRM_RN_MAXREGS));
 }
 
 template <int VPL, int MODE, bool HAS_W>
@@ -438,7 +446,7 @@ struct RowArgsF32 {
 };
 
 template <int VPL, bool HAS_W>
-__global__ void __launch_bounds__(kThreads, HRM_RN_F32_MINBLOCKS) rms_f32_warp_kernel(const RowArgsF32 a) {
+__global__ void __launch_bounds__(kThreads, min_blocks_for(HRM_RN_F32_MAXREGS)) rms_f32_warp_kernel(const RowArgsF32 a) {
   grid_dependency_begin();
   extern __shared__ uint4 s_w4[];
   float4* s_w = reinterpret_cast<float4*>(s_w4);
