@@ -67,13 +67,14 @@ struct RopeArgs {
   int64_t batch_stride, pos_stride, head_stride;
   const float4* table;  // [positions][head_dim] floats: cos in [0, hd/2), sin in [hd/2, hd)
   int64_t seq;
-  int64_t tiles_per_batch;
-  int64_t ntiles;
+  int tiles_per_batch;  // tile counts fit 31 bits (checked at launch): 32-bit index math
+  int ntiles;
   int heads;
   int head_dim;
-  int g;   // threads per row (= chunks per half-row)
-  int pt;  // positions per tile
-  int ht;  // head slices per tile
+  int g;   // threads per row (= chunks per half-row), a power of two
+  int pt;  // positions per tile, a power of two
+  int ht;  // head slices per tile, a power of two
+  int lg, lht;  // log2(g), log2(ht)
   int offset;
   float theta;
 };
@@ -125,17 +126,22 @@ __device__ __forceinline__ void load_cos_sin(const float4* table, int pos, int j
   }
 }
 
+// Thread layout within a tile (g, ht powers of two): lane j of its row, head
+// slice, position in the tile.  Shifts and masks, and 32-bit tile arithmetic:
+// at decode sizes a launch is a handful of CTAs whose time is latency, where a
+// 64-bit division costs a visible fraction.
 template <bool TABLE>
 __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel(const RopeArgs a) {
   grid_dependency_begin();
-  const int j = threadIdx.x % a.g;
-  const int rest = threadIdx.x / a.g;
-  const int slice = rest % a.ht;
-  const int pl = rest / a.ht;
+  const int j = threadIdx.x & (a.g - 1);
+  const int rest = threadIdx.x >> a.lg;
+  const int slice = rest & (a.ht - 1);
+  const int pl = rest >> a.lht;
 
-  for (int64_t tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
-    const int64_t b = tile / a.tiles_per_batch;
-    const int64_t s = (tile - b * a.tiles_per_batch) * a.pt + pl;
+  for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
+    const int bi = tile / a.tiles_per_batch;
+    const int64_t b = bi;
+    const int64_t s = (int64_t)(tile - bi * a.tiles_per_batch) * a.pt + pl;
     if (s >= a.seq) continue;
     const int pos = (int)s + a.offset;
 
@@ -245,13 +251,14 @@ struct SplitArgs {
   uint4* vc;  // v cache or null
   const float4* table;
   int64_t seq;
-  int64_t tiles_per_batch;
-  int64_t ntiles;
+  int tiles_per_batch;  // 31-bit tile counts, as RopeArgs
+  int ntiles;
   int64_t cache_len;
   int64_t cache_offset;
   int heads;
   int head_dim;
   int g, pt, ht;
+  int lg, lht;  // log2(g), log2(ht)
   int offset;
   float theta;
 };
@@ -259,16 +266,17 @@ struct SplitArgs {
 template <bool TABLE, bool CACHE>
 __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) split_rope_tile_kernel(const SplitArgs a) {
   grid_dependency_begin();
-  const int j = threadIdx.x % a.g;
-  const int rest = threadIdx.x / a.g;
-  const int slice = rest % a.ht;
-  const int pl = rest / a.ht;
+  const int j = threadIdx.x & (a.g - 1);
+  const int rest = threadIdx.x >> a.lg;
+  const int slice = rest & (a.ht - 1);
+  const int pl = rest >> a.lht;
   const int row_chunks = 2 * a.g;                       // 16-byte chunks per head row
   const int64_t seg = (int64_t)a.heads * row_chunks;   // chunks per gqkv segment
 
-  for (int64_t tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
-    const int64_t b = tile / a.tiles_per_batch;
-    const int64_t s = (tile - b * a.tiles_per_batch) * a.pt + pl;
+  for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
+    const int bi = tile / a.tiles_per_batch;
+    const int64_t b = bi;
+    const int64_t s = (int64_t)(tile - bi * a.tiles_per_batch) * a.pt + pl;
     if (s >= a.seq) continue;
     float c[8], sn[8];
     load_cos_sin<TABLE>(a.table, (int)s + a.offset, j, a.head_dim, a.theta, c, sn);
@@ -365,6 +373,16 @@ int pow2_ceil(int64_t x) {
   return p;
 }
 
+int log2_of(int p) {  // p a power of two
+  int l = 0;
+  while ((1 << l) < p) ++l;
+  return l;
+}
+
+// Tile counts the tiled kernels take: their 32-bit tile loop needs
+// ntiles + gridDim.x < 2^31.
+constexpr int64_t kMaxTiles = (int64_t)1 << 30;
+
 }  // namespace
 
 cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
@@ -372,8 +390,13 @@ cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t 
   cudaError_t err = cudaSuccess;
   const int64_t sms = device_sm_count();
   const int g = (int)(head_dim / 16);
+  int pt = pow2_ceil(seq);
+  if (pt > kThreads / (g > 0 ? g : 1)) pt = kThreads / (g > 0 ? g : 1);
+  if (pt > HRM_ROPE_MAX_PT) pt = HRM_ROPE_MAX_PT;
+  const int64_t tiles_per_batch = (seq + pt - 1) / pt;
   const bool fast = head_dim % 16 == 0 && head_dim <= 512 && (g & (g - 1)) == 0 && aligned16(q) &&
-                    aligned16(k) && (table == nullptr || aligned16(table));
+                    aligned16(k) && (table == nullptr || aligned16(table)) &&
+                    batch <= kMaxTiles / tiles_per_batch;
   if (fast) {
     RopeArgs a;
     a.q = static_cast<uint4*>(q);
@@ -387,12 +410,12 @@ cudaError_t launch_rope(void* q, void* k, int64_t batch, int64_t heads, int64_t 
     a.heads = (int)heads;
     a.head_dim = (int)head_dim;
     a.g = g;
-    a.pt = pow2_ceil(seq);
-    if (a.pt > kThreads / g) a.pt = kThreads / g;
-    if (a.pt > HRM_ROPE_MAX_PT) a.pt = HRM_ROPE_MAX_PT;
+    a.pt = pt;
     a.ht = kThreads / (g * a.pt);
-    a.tiles_per_batch = (seq + a.pt - 1) / a.pt;
-    a.ntiles = batch * a.tiles_per_batch;
+    a.lg = log2_of(g);
+    a.lht = log2_of(a.ht);
+    a.tiles_per_batch = (int)tiles_per_batch;
+    a.ntiles = (int)(batch * tiles_per_batch);
     a.offset = (int)offset;
     a.theta = theta;
     int64_t blocks = a.ntiles;
@@ -428,9 +451,14 @@ cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, vo
   cudaError_t err = cudaSuccess;
   const int64_t sms = device_sm_count();
   const int g = (int)(head_dim / 16);
+  int pt = pow2_ceil(seq);
+  if (pt > kThreads / (g > 0 ? g : 1)) pt = kThreads / (g > 0 ? g : 1);
+  if (pt > HRM_ROPE_MAX_PT) pt = HRM_ROPE_MAX_PT;
+  const int64_t tiles_per_batch = (seq + pt - 1) / pt;
   const bool fast = head_dim % 16 == 0 && head_dim <= 512 && (g & (g - 1)) == 0 && aligned16(gqkv) &&
                     aligned16(gate) && aligned16(q) && aligned16(k) && aligned16(v) &&
-                    (kc == nullptr || (aligned16(kc) && aligned16(vc))) && (table == nullptr || aligned16(table));
+                    (kc == nullptr || (aligned16(kc) && aligned16(vc))) && (table == nullptr || aligned16(table)) &&
+                    batch <= kMaxTiles / tiles_per_batch;
   if (fast) {
     SplitArgs a;
     a.gqkv = static_cast<const uint4*>(gqkv);
@@ -445,12 +473,12 @@ cudaError_t launch_split_rope(const void* gqkv, void* gate, void* q, void* k, vo
     a.heads = (int)heads;
     a.head_dim = (int)head_dim;
     a.g = g;
-    a.pt = pow2_ceil(seq);
-    if (a.pt > kThreads / g) a.pt = kThreads / g;
-    if (a.pt > HRM_ROPE_MAX_PT) a.pt = HRM_ROPE_MAX_PT;
+    a.pt = pt;
     a.ht = kThreads / (g * a.pt);
-    a.tiles_per_batch = (seq + a.pt - 1) / a.pt;
-    a.ntiles = batch * a.tiles_per_batch;
+    a.lg = log2_of(g);
+    a.lht = log2_of(a.ht);
+    a.tiles_per_batch = (int)tiles_per_batch;
+    a.ntiles = (int)(batch * tiles_per_batch);
     a.cache_len = cache_len;
     a.cache_offset = cache_offset;
     a.offset = (int)offset;
