@@ -19,10 +19,12 @@
 // any store.
 //
 // Angles: either the fp32 table written by rope_table_kernel or, with no
-// table, evaluated in the thread with exactly the reference expression
+// table, evaluated in the kernel with exactly the reference expression
 //   (float)(s + offset) * expf(-2.0f * i * logf(theta) / (float)head_dim)
-// and sincosf (src/kernels/rope_embed.cu:41-43).  The table is built with that
-// same expression, so both ways give the reference's cos/sin bit for bit.
+// and sincosf (src/kernels/rope_embed.cu:41-43), each of a tile's distinct
+// angles once, shared through shared memory (tile_angles).  The table is
+// built with that same expression, so both ways give the reference's cos/sin
+// bit for bit.
 // The rotation is written with explicit roundings in the forms nvcc gives the
 // reference's source (src/kernels/rope_embed.cu:45-53), established by
 // running the reference kernel against every candidate rounding:
@@ -110,20 +112,40 @@ __device__ __forceinline__ void rotate8(uint4& lo, uint4& hi, const float (&c)[8
   }
 }
 
-// cos/sin of pairs 8j..8j+7 at position pos: from the table or in-kernel.
-template <bool TABLE>
-__device__ __forceinline__ void load_cos_sin(const float4* table, int pos, int j, int head_dim, float theta,
-                                             float (&c)[8], float (&sn)[8]) {
-  if (TABLE) {
-    const float4* row = table + (int64_t)pos * (head_dim / 4);
-    const float4 c0 = ld_keep(row + 2 * j), c1 = ld_keep(row + 2 * j + 1);
-    const float4 s0 = ld_keep(row + head_dim / 8 + 2 * j), s1 = ld_keep(row + head_dim / 8 + 2 * j + 1);
-    c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
-    sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) sincosf(rope_angle(pos, 8 * j + e, head_dim, theta), &sn[e], &c[e]);
+// cos/sin of pairs 8j..8j+7 at position pos from the table.
+__device__ __forceinline__ void table_cos_sin(const float4* table, int pos, int j, int head_dim, float (&c)[8],
+                                              float (&sn)[8]) {
+  const float4* row = table + (int64_t)pos * (head_dim / 4);
+  const float4 c0 = ld_keep(row + 2 * j), c1 = ld_keep(row + 2 * j + 1);
+  const float4 s0 = ld_keep(row + head_dim / 8 + 2 * j), s1 = ld_keep(row + head_dim / 8 + 2 * j + 1);
+  c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+  sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+}
+
+// In-kernel angles (no table): the tile's distinct (position, pair) angles
+// are shared out -- each of the CTA's threads evaluates one at a time, with
+// the reference expression and sincosf, into shared memory -- instead of every
+// thread evaluating the 8 of its own pairs, which all the tile's head slices
+// repeat.  A decode tile (1 position, 64 pairs for head_dim 128) thus costs
+// one sincosf per thread instead of 8.  Positions past seq are skipped.
+constexpr int kMaxAngles = HRM_ROPE_MAX_PT * 256;  // tile positions x pairs (head_dim <= 512)
+
+__device__ __forceinline__ void tile_angles(float* s_cos, float* s_sin, int64_t s_base, int64_t seq, int pt,
+                                            int lhalf, int offset, int head_dim, float theta) {
+  const int half = 1 << lhalf;
+  for (int idx = threadIdx.x; idx < (pt << lhalf); idx += blockDim.x) {
+    const int p = idx >> lhalf, i = idx & (half - 1);
+    if (s_base + p < seq) sincosf(rope_angle((int)(s_base + p) + offset, i, head_dim, theta), &s_sin[idx], &s_cos[idx]);
   }
+}
+
+__device__ __forceinline__ void shared_cos_sin(const float* s_cos, const float* s_sin, int pl, int j, int lhalf,
+                                               float (&c)[8], float (&sn)[8]) {
+  const float4* cr = reinterpret_cast<const float4*>(s_cos + (pl << lhalf) + 8 * j);
+  const float4* sr = reinterpret_cast<const float4*>(s_sin + (pl << lhalf) + 8 * j);
+  const float4 c0 = cr[0], c1 = cr[1], s0 = sr[0], s1 = sr[1];
+  c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+  sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
 }
 
 // Thread layout within a tile (g, ht powers of two): lane j of its row, head
@@ -138,15 +160,25 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel
   const int slice = rest & (a.ht - 1);
   const int pl = rest >> a.lht;
 
+  __shared__ __align__(16) float s_cos[TABLE ? 1 : kMaxAngles], s_sin[TABLE ? 1 : kMaxAngles];
   for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
     const int bi = tile / a.tiles_per_batch;
     const int64_t b = bi;
-    const int64_t s = (int64_t)(tile - bi * a.tiles_per_batch) * a.pt + pl;
+    const int64_t s_base = (int64_t)(tile - bi * a.tiles_per_batch) * a.pt;
+    const int64_t s = s_base + pl;
+    if (!TABLE) {
+      __syncthreads();  // the previous tile's angles are no longer read
+      tile_angles(s_cos, s_sin, s_base, a.seq, a.pt, a.lg + 3, a.offset, a.head_dim, a.theta);
+      __syncthreads();
+    }
     if (s >= a.seq) continue;
     const int pos = (int)s + a.offset;
 
     float c[8], sn[8];
-    load_cos_sin<TABLE>(a.table, pos, j, a.head_dim, a.theta, c, sn);
+    if (TABLE)
+      table_cos_sin(a.table, pos, j, a.head_dim, c, sn);
+    else
+      shared_cos_sin(s_cos, s_sin, pl, j, a.lg + 3, c, sn);
 
     const int64_t head_step = a.head_stride;
     const int64_t row0 = b * a.batch_stride + s * a.pos_stride + j;
@@ -273,13 +305,23 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) split_rope_tile_
   const int row_chunks = 2 * a.g;                       // 16-byte chunks per head row
   const int64_t seg = (int64_t)a.heads * row_chunks;   // chunks per gqkv segment
 
+  __shared__ __align__(16) float s_cos[TABLE ? 1 : kMaxAngles], s_sin[TABLE ? 1 : kMaxAngles];
   for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
     const int bi = tile / a.tiles_per_batch;
     const int64_t b = bi;
-    const int64_t s = (int64_t)(tile - bi * a.tiles_per_batch) * a.pt + pl;
+    const int64_t s_base = (int64_t)(tile - bi * a.tiles_per_batch) * a.pt;
+    const int64_t s = s_base + pl;
+    if (!TABLE) {
+      __syncthreads();  // the previous tile's angles are no longer read
+      tile_angles(s_cos, s_sin, s_base, a.seq, a.pt, a.lg + 3, a.offset, a.head_dim, a.theta);
+      __syncthreads();
+    }
     if (s >= a.seq) continue;
     float c[8], sn[8];
-    load_cos_sin<TABLE>(a.table, (int)s + a.offset, j, a.head_dim, a.theta, c, sn);
+    if (TABLE)
+      table_cos_sin(a.table, (int)s + a.offset, j, a.head_dim, c, sn);
+    else
+      shared_cos_sin(s_cos, s_sin, pl, j, a.lg + 3, c, sn);
 
     const int64_t tok = b * a.seq + s;
     const int64_t in0 = tok * 4 * seg + j;                              // + h * row_chunks
