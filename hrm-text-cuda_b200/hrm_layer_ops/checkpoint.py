@@ -330,8 +330,10 @@ def _upload(path, chunks, device, chunk_bytes, reader_threads, stream):
                 ev = torch.cuda.Event()
                 ev.record(s)
                 events[r] = ev
-            s.synchronize()
     finally:
+        # Also on an error: the pinned buffers go back to torch's allocator,
+        # which does not know that copies queued through the C ABI read them.
+        s.synchronize()
         os.close(fd)
 
 
