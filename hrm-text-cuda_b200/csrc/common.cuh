@@ -60,6 +60,16 @@ __device__ __forceinline__ void grid_dependency_begin() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
+// L2 prefetch of `bytes` (a multiple of 16) at the 16-byte aligned address p,
+// by the bulk-copy engine.  A kernel may issue it BEFORE grid_dependency_begin
+// for inputs the previous grid may still be writing: L2 is the point of
+// coherence for global memory, so the prefetch can only warm lines -- the
+// loads issued after the wait still see the previous grid's writes -- while
+// the DRAM reads start during the previous grid's drain instead of after it.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------- async staging
 // cp.async (LDGSTS) of one 16-byte chunk global -> shared, L2-cached only.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {

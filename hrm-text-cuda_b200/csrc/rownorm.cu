@@ -210,8 +210,21 @@ constexpr int rownorm_min_blocks() {
   return min_blocks_for((MODE == kAdd && VPL > 8) ? 255 : ((MODE != kAdd && VPL <= 6) ? 64 : HRM_RN_MAXREGS));
 }
 
+// L2 prefetch of each warp's first row(s) before the grid dependency wait
+// (1) or none (0).
+#ifndef HRM_RN_PREFETCH
+#define HRM_RN_PREFETCH 1
+#endif
+
 template <int VPL, int MODE, bool HAS_W>
 __global__ void __launch_bounds__(kThreads, rownorm_min_blocks<VPL, MODE>()) rownorm_warp_kernel(const RowArgs a) {
+  if (HRM_RN_PREFETCH && MODE != kEmbed && (threadIdx.x & 31) == 0) {
+    const int64_t r0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r0 < a.rows) {
+      prefetch_l2(a.x + r0 * a.nchunks, (uint32_t)a.nchunks * 16u);
+      if (MODE == kAdd) prefetch_l2(a.b + r0 * a.nchunks, (uint32_t)a.nchunks * 16u);
+    }
+  }
   grid_dependency_begin();
   extern __shared__ uint4 s_w[];
   const int lane = threadIdx.x & 31;
@@ -447,6 +460,10 @@ struct RowArgsF32 {
 
 template <int VPL, bool HAS_W>
 __global__ void __launch_bounds__(kThreads, min_blocks_for(HRM_RN_F32_MAXREGS)) rms_f32_warp_kernel(const RowArgsF32 a) {
+  if (HRM_RN_PREFETCH && (threadIdx.x & 31) == 0) {  // first row, as the bf16 kernel
+    const int64_t r0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r0 < a.rows) prefetch_l2(a.x + r0 * a.nchunks, (uint32_t)a.nchunks * 16u);
+  }
   grid_dependency_begin();
   extern __shared__ uint4 s_w4[];
   float4* s_w = reinterpret_cast<float4*>(s_w4);
