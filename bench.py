@@ -956,8 +956,12 @@ def run_ours(args, world, rank, device, peers):
     else:
         kern_ms = {k: sum(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps)) / args.steps
                    for j, k in enumerate(wl.kernels)}
+    per_rank_ms = None
     if world > 1:
         t = torch.tensor([ms_total] + [kern_ms[k] for k in wl.kernels], device=device, dtype=torch.float64)
+        every = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(every, t)
+        per_rank_ms = [round(float(x[0]) / args.steps, 4) for x in every]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t[0])
         kern_ms = {k: float(t[j + 1]) for j, k in enumerate(wl.kernels)}
@@ -1020,6 +1024,8 @@ def run_ours(args, world, rank, device, peers):
         "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
+    if per_rank_ms is not None:
+        line["per_rank_ms_per_step"] = per_rank_ms  # each rank's own device time; value uses the max
     if decode_us is not None:
         line["decode_64_tokens_us"] = round(decode_us, 2)  # median of 5 x 200 graph replays
         line["decode_64_tokens_us_range"] = [round(v, 2) for v in decode_range]
