@@ -600,8 +600,11 @@ class LoadCheckpoint:
         self.torch, self.ck, self.ops, self.device = torch, ck, ops, device
         self.own_dir = None
         if path is None:
+            import atexit
+
             base = "/dev/shm" if os.path.isdir("/dev/shm") else None
             self.own_dir = tempfile.mkdtemp(prefix="hrm_ckpt_", dir=base)
+            atexit.register(self.close)  # the 4.7 GB file goes even if the run fails
             path = os.path.join(self.own_dir, "model.safetensors")
             self._write(path, dtype, np)
         self.path = path
@@ -702,6 +705,7 @@ class LoadCheckpoint:
 
         if self.own_dir is not None:
             shutil.rmtree(self.own_dir, ignore_errors=True)
+            self.own_dir = None
 
     def step(self, stream=None, events=None):
         if events is not None:
