@@ -571,6 +571,73 @@ class SingleOp:
         return None
 
 
+# The reference model's shapes (HrmConfig defaults, src/lib.rs:40-60).
+CKPT_LAYERS, CKPT_H, CKPT_I, CKPT_V = 16, 1536, 4096, 65536
+
+
+def write_synthetic_checkpoint(path, dtype="F32"):
+    """A safetensors file of the reference model's tensors (the names of
+    src/lib.rs:2043-2112, attention / MLP prefixes), values 0.02 N(0, 1) from a
+    16 MB seeded block repeated."""
+    import json
+
+    import numpy as np
+
+    es = {"F32": 4, "BF16": 2, "F16": 2}[dtype]
+    L, H, I, V = CKPT_LAYERS, CKPT_H, CKPT_I, CKPT_V
+    shapes = []
+    for mod in ("H", "L"):
+        for i in range(L):
+            p = f"model.{mod}_module.layers.{i}"
+            shapes += [(f"{p}.attn.gqkv_proj.weight", (4 * H, H)), (f"{p}.attn.o_proj.weight", (H, H)),
+                       (f"{p}.mlp.gate_up_proj.weight", (2 * I, H)), (f"{p}.mlp.down_proj.weight", (H, I))]
+    shapes += [("model.embed_tokens.weight", (V, H)), ("lm_head.weight", (V, H)), ("model.z_L_init", (H,))]
+    header, off = {}, 0
+    for name, shape in shapes:
+        n = int(np.prod(shape)) * es
+        header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [off, off + n]}
+        off += n
+    text = json.dumps(header).encode()
+    text += b" " * (-len(text) % 8)
+    block = (np.random.default_rng(0).standard_normal(1 << 22) * 0.02).astype(
+        {"F32": np.float32, "F16": np.float16, "BF16": np.float32}[dtype])
+    if dtype == "BF16":
+        block = (block.view(np.uint32) >> 16).astype(np.uint16)
+    block = block.tobytes()
+    with open(path, "wb") as f:
+        f.write(len(text).to_bytes(8, "little"))
+        f.write(text)
+        left = off
+        while left > 0:
+            k = min(left, len(block))
+            f.write(block[:k])
+            left -= k
+
+
+def checkpoint_config(dtype, file_bytes, pieces, bytes_per_step):
+    """The load_checkpoint workload's `config`, the same dict on both arms."""
+    return {"workload": "checkpoint file -> bf16 device tensors, HRM-Text-1B shapes "
+                        f"({CKPT_LAYERS} layers x 2 modules, hidden {CKPT_H}, intermediate {CKPT_I}, "
+                        f"vocab {CKPT_V})", "dtype_in_file": dtype, "file_bytes": file_bytes,
+            "tensor_pieces": pieces,
+            "l2": f"{bytes_per_step / 1e9:.1f} GB moved per step vs 126 MB L2; no flush"}
+
+
+def temp_checkpoint(owner, dtype):
+    """Writes the synthetic checkpoint into a fresh directory (in /dev/shm
+    where there is one), removed at exit even after a failure; returns its path
+    and sets owner.own_dir."""
+    import atexit
+    import tempfile
+
+    base = "/dev/shm" if os.path.isdir("/dev/shm") else None
+    owner.own_dir = tempfile.mkdtemp(prefix="hrm_ckpt_", dir=base)
+    atexit.register(owner.close)
+    path = os.path.join(owner.own_dir, "model.safetensors")
+    write_synthetic_checkpoint(path, dtype)
+    return path
+
+
 class LoadCheckpoint:
     """Checkpoint file -> bf16 device tensors at the reference model's shapes
     (HrmConfig defaults, src/lib.rs:40-60: 16 layers per module, hidden 1536,
@@ -586,11 +653,9 @@ class LoadCheckpoint:
     z_L_init; file_gbs is the file's bytes over that time."""
 
     name = "load_checkpoint"
-    LAYERS, H, I, V = 16, 1536, 4096, 65536
+    LAYERS, H, I, V = CKPT_LAYERS, CKPT_H, CKPT_I, CKPT_V
 
     def __init__(self, device, rank, path=None, dtype="F32"):
-        import tempfile
-
         import numpy as np
         import torch
 
@@ -600,13 +665,7 @@ class LoadCheckpoint:
         self.torch, self.ck, self.ops, self.device = torch, ck, ops, device
         self.own_dir = None
         if path is None:
-            import atexit
-
-            base = "/dev/shm" if os.path.isdir("/dev/shm") else None
-            self.own_dir = tempfile.mkdtemp(prefix="hrm_ckpt_", dir=base)
-            atexit.register(self.close)  # the 4.7 GB file goes even if the run fails
-            path = os.path.join(self.own_dir, "model.safetensors")
-            self._write(path, dtype, np)
+            path = temp_checkpoint(self, dtype)  # removed at exit even if the run fails
         self.path = path
         self.hdr = ck.read_header(path)
         hdr = self.hdr
@@ -632,46 +691,8 @@ class LoadCheckpoint:
         self.dominant = "convert_to_bf16"
         self.kernel_bytes = {"convert_to_bf16": self.bytes_per_step}
         self.footprint = self.bytes_per_step
-        self.config = {"workload": "checkpoint file -> bf16 device tensors, HRM-Text-1B shapes "
-                                   f"({self.LAYERS} layers x 2 modules, hidden {self.H}, intermediate {self.I}, "
-                                   f"vocab {self.V})", "dtype_in_file": dtype, "file_bytes": size,
-                       "tensor_pieces": len(self.pieces),
-                       "l2": f"{self.bytes_per_step / 1e9:.1f} GB moved per step vs 126 MB L2; no flush",
-                       "launch": "the step's conversions captured in a CUDA graph, replayed between the events"}
+        self.config = checkpoint_config(dtype, size, len(self.pieces), self.bytes_per_step)
         self.data = "synthetic safetensors file (f32, 0.02 N(0,1) tiled), written once per run"
-
-    def _write(self, path, dtype, np):
-        import json
-
-        es = {"F32": 4, "BF16": 2, "F16": 2}[dtype]
-        L, H, I, V = self.LAYERS, self.H, self.I, self.V
-        shapes = []
-        for mod in ("H", "L"):
-            for i in range(L):
-                p = f"model.{mod}_module.layers.{i}"
-                shapes += [(f"{p}.attn.gqkv_proj.weight", (4 * H, H)), (f"{p}.attn.o_proj.weight", (H, H)),
-                           (f"{p}.mlp.gate_up_proj.weight", (2 * I, H)), (f"{p}.mlp.down_proj.weight", (H, I))]
-        shapes += [("model.embed_tokens.weight", (V, H)), ("lm_head.weight", (V, H)), ("model.z_L_init", (H,))]
-        header, off = {}, 0
-        for name, shape in shapes:
-            n = int(np.prod(shape)) * es
-            header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [off, off + n]}
-            off += n
-        text = json.dumps(header).encode()
-        text += b" " * (-len(text) % 8)
-        block = (np.random.default_rng(0).standard_normal(1 << 22) * 0.02).astype(
-            {"F32": np.float32, "F16": np.float16, "BF16": np.float32}[dtype])
-        if dtype == "BF16":
-            block = (block.view(np.uint32) >> 16).astype(np.uint16)
-        block = block.tobytes()
-        with open(path, "wb") as f:
-            f.write(len(text).to_bytes(8, "little"))
-            f.write(text)
-            left = off
-            while left > 0:
-                k = min(left, len(block))
-                f.write(block[:k])
-                left -= k
 
     def cpu_sample(self, min_seconds=5.0, sample_bytes=512 << 20):
         """The reference's host conversion (raw_to_bf16, restated by the oracle,
@@ -815,14 +836,104 @@ class Module:
 
 
 # ------------------------------------------------------------------ main
+class ReferenceCheckpointLoad:
+    """The reference's load_safetensors path (src/lib.rs:2023-2125) on the host:
+    the whole file read into memory (std::fs::read), every tensor converted to
+    bf16 on the host (raw_to_bf16, src/lib.rs:1981-2008, restated by the oracle
+    with all host threads), gate_up split into two host copies
+    (src/lib.rs:2072-2078), and each tensor copied to the GPU from pageable
+    memory (cudarc's htod_copy; a torch copy here).  Imports nothing of the
+    library."""
+
+    def __init__(self, path=None, dtype="F32"):
+        import numpy as np
+
+        sys.path.insert(0, ROOT)
+        from oracle import Oracle
+
+        self.np = np
+        self.o = Oracle()
+        self.o.set_threads(len(os.sched_getaffinity(0)))
+        self.cores = self.o.max_threads()
+        self.own_dir = None
+        self.path = path if path is not None else temp_checkpoint(self, dtype)
+        self.dtype = dtype
+        with open(self.path, "rb") as f:
+            n = int.from_bytes(f.read(8), "little")
+            self.header = {k: v for k, v in json.loads(f.read(n)).items() if k != "__metadata__"}
+        self.base = 8 + n
+        self.file_bytes = os.path.getsize(self.path)
+        sizes = {"F32": 4, "F16": 2, "BF16": 2}
+        self.bytes_per_step, self.pieces = 0, 0
+        for name, t in self.header.items():
+            numel = (t["data_offsets"][1] - t["data_offsets"][0]) // sizes[t["dtype"]]
+            self.bytes_per_step += numel * (sizes[t["dtype"]] + 2)
+            self.pieces += 2 if name.endswith("gate_up_proj.weight") else 1
+
+    def run_once(self):
+        import torch
+
+        np = self.np
+        with open(self.path, "rb") as f:
+            data = f.read()
+        split = CKPT_I * CKPT_H
+        out = []
+        for name, t in self.header.items():
+            b0, b1 = self.base + t["data_offsets"][0], self.base + t["data_offsets"][1]
+            host = self.o.convert_to_bf16(data[b0:b1], t["dtype"].lower())
+            parts = [host[:split].copy(), host[split:].copy()] if name.endswith("gate_up_proj.weight") else [host]
+            for h in parts:
+                out.append(torch.from_numpy(h.view(np.int16)).to("cuda"))
+        torch.cuda.synchronize()
+        return out
+
+    def close(self):
+        import shutil
+
+        if self.own_dir is not None:
+            shutil.rmtree(self.own_dir, ignore_errors=True)
+            self.own_dir = None
+
+
+def reference_checkpoint_arm(args, world):
+    c = ReferenceCheckpointLoad(args.ckpt)
+    try:
+        for _ in range(args.warmup):
+            c.run_once()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            c.run_once()
+        sec = (time.perf_counter() - t0) / args.steps
+    finally:
+        c.close()
+    gbs = c.bytes_per_step / sec / 1e9
+    sample = (f"whole loads of the {c.file_bytes / 1e9:.2f} GB synthetic checkpoint: file read, host conversion "
+              f"(oracle, {c.cores} OpenMP threads), gate_up split, pageable copies to the GPU")
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1000, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 math)",
+        "data": "synthetic safetensors file (f32, 0.02 N(0,1) tiled), written once per run",
+        "config": checkpoint_config(c.dtype, c.file_bytes, c.pieces, c.bytes_per_step),
+        "file_gbs": round(c.file_bytes / sec / 1e9, 3),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": c.cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def reference_arm(args, world, rank):
     """The reference's path on the host cores: the oracle, all threads, over the
     whole pass of the GPU arm's workload (rank 0's shard of --tokens tokens).
     Imports nothing of the library (neither hrm_layer_ops nor libhrm_ops.so)."""
     if rank != 0:
         return
+    if args.workload == "load_checkpoint":
+        reference_checkpoint_arm(args, world)
+        return
     if args.workload != "chain":
-        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the chain workload"}))
+        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the chain and "
+                                                                "load_checkpoint workloads"}))
         return
     token_major = args.qk_layout == "token"
     c = CpuChain(args.tokens, token_major)
