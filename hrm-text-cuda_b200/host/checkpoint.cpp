@@ -11,6 +11,7 @@
 // while the GPU copies the previous one.  gate_up's two halves go straight to
 // gate_proj and up_proj.
 #include <fcntl.h>
+#include <sched.h>
 #include <unistd.h>
 
 #include <algorithm>
@@ -120,7 +121,11 @@ HrmLayerOps::ModelWeights HrmLayerOps::load_safetensors(const std::string& path,
            std::string("unsupported dtype ") + st_dtype_name(t.dtype) + " of tensor " + t.name);
   if (chunk_bytes < 64) chunk_bytes = 64;
   chunk_bytes = chunk_bytes / 16 * 16;
-  if (reader_threads < 1) reader_threads = 1;
+  if (reader_threads < 1) {
+    cpu_set_t set;
+    reader_threads = sched_getaffinity(0, sizeof(set), &set) == 0 ? CPU_COUNT(&set) : 1;
+    reader_threads = std::max(1, std::min(16, reader_threads));
+  }
 
   std::vector<Piece> pieces;
   auto tensor = [&](const std::string& name) -> const StTensor& {

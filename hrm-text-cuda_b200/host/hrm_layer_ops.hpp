@@ -161,8 +161,9 @@ class HrmLayerOps {
   // missing tensor, a gate_up smaller than its gate half, or any tensor of a
   // dtype other than BF16 / F32 / F16 (the reference converts every tensor
   // of the file and panics on those).
-  ModelWeights load_safetensors(const std::string& path, size_t chunk_bytes = 64u << 20,
-                                int reader_threads = 8) const;
+  // reader_threads 0: one per core this process may use, at most 16.
+  ModelWeights load_safetensors(const std::string& path, size_t chunk_bytes = 128u << 20,
+                                int reader_threads = 0) const;
 
   // ---- fused entry points that replace wrapper sequences of the reference
   // additive_inject -> rms_norm (src/lib.rs:976-979); weight may be null.
