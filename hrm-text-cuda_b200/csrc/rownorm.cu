@@ -66,8 +66,8 @@ namespace {
 constexpr int kWarps = HRM_RN_WARPS;          // warp-per-row kernels
 constexpr int kThreads = 32 * kWarps;
 // __launch_bounds__ minimum resident CTAs that caps a thread at max_regs.
-constexpr int min_blocks_for(int max_regs) {
-  return 65536 / (kThreads * max_regs) < 1 ? 1 : 65536 / (kThreads * max_regs);
+constexpr int min_blocks_for(int max_regs, int threads = kThreads) {
+  return 65536 / (threads * max_regs) < 1 ? 1 : 65536 / (threads * max_regs);
 }
 constexpr int kBlockThreads = 256;            // reference-shaped fallback: 8 warps per row
 constexpr int kBlockWarps = kBlockThreads / 32;
@@ -199,15 +199,38 @@ __device__ __forceinline__ void publish_weight() {
   __syncthreads();
 }
 
+// Register cap of plain RMSNorm over rows of 1544-2048 elements (7-8 chunks
+// per lane; 64 holds the row without spilling) and its warps per CTA, used
+// where the launch then fits in one wave; and the cap of embed + RMSNorm there.
+#ifndef HRM_RN_NORM8_MAXREGS
+#define HRM_RN_NORM8_MAXREGS 64
+#endif
+#ifndef HRM_RN_NORM8_WARPS
+#define HRM_RN_NORM8_WARPS 8
+#endif
+#ifndef HRM_RN_EMBED8_MAXREGS
+#define HRM_RN_EMBED8_MAXREGS HRM_RN_MAXREGS
+#endif
+
 // Register cap: HRM_RN_MAXREGS, except
 // - add + RMSNorm over rows of more than 2048 elements, whose x and branch
 //   chunks (2 x 16 per lane) need more registers than that without spilling;
 // - plain and embed + RMSNorm over rows of at most 1536 elements (<= 6 chunks
 //   per lane), capped at 64 registers for more warps per SM: embed + RMSNorm
-//   at the reference model's hidden 1536 measured 6.36 -> 6.46 TB/s with it.
+//   at the reference model's hidden 1536 measured 6.36 -> 6.46 TB/s with it;
+// - plain RMSNorm over rows of 1544-2048 elements, capped at 64 in 8-warp CTAs
+//   when the launch then fits in one wave (4 CTAs per SM): a [4096 x 2048]
+//   launch (512 CTAs) is one wave on 148 SMs, against 1.15 waves in the
+//   default shape (80 registers, 4-warp CTAs).  Back to back on B200: 7.00 us
+//   default, 6.39 us capped in 4-warp CTAs (1024 of them, also one wave), 6.23
+//   us capped in 8-warp CTAs.  Larger launches keep the default shape (65536
+//   rows: 79.0 us, against 79.4 us capped).  The choice is made per launch.
 template <int VPL, int MODE>
-constexpr int rownorm_min_blocks() {
-  return min_blocks_for((MODE == kAdd && VPL > 8) ? 255 : ((MODE != kAdd && VPL <= 6) ? 64 : HRM_RN_MAXREGS));
+constexpr int rownorm_max_regs() {
+  return MODE == kAdd ? (VPL > 8 ? 255 : HRM_RN_MAXREGS)
+         : VPL <= 6   ? 64
+         : VPL <= 8   ? (MODE == kRms ? HRM_RN_MAXREGS : HRM_RN_EMBED8_MAXREGS)
+                      : HRM_RN_MAXREGS;
 }
 
 // L2 prefetch of each warp's first row(s) before the grid dependency wait
@@ -216,8 +239,9 @@ constexpr int rownorm_min_blocks() {
 #define HRM_RN_PREFETCH 1
 #endif
 
-template <int VPL, int MODE, bool HAS_W>
-__global__ void __launch_bounds__(kThreads, rownorm_min_blocks<VPL, MODE>()) rownorm_warp_kernel(const RowArgs a) {
+template <int VPL, int MODE, bool HAS_W, int REGS = rownorm_max_regs<VPL, MODE>(), int WARPS = kWarps>
+__global__ void __launch_bounds__(32 * WARPS, min_blocks_for(REGS, 32 * WARPS))
+    rownorm_warp_kernel(const RowArgs a) {
   if (HRM_RN_PREFETCH && MODE != kEmbed && (threadIdx.x & 31) == 0) {
     const int64_t r0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r0 < a.rows) {
@@ -230,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, rownorm_min_blocks<VPL, MODE>()) row
   const int lane = threadIdx.x & 31;
   if (HAS_W) issue_weight(s_w, a.w, a.nchunks);
 
-  const int nwarps = blockDim.x >> 5;  // kWarps, or fewer for a small launch
+  const int nwarps = blockDim.x >> 5;  // WARPS, or fewer for a small launch
   const int64_t warp_stride = (int64_t)gridDim.x * nwarps;
   int64_t row = (int64_t)blockIdx.x * nwarps + (threadIdx.x >> 5);
   for (bool first = true; first || row < a.rows; first = false, row += warp_stride) {
@@ -603,28 +627,41 @@ __global__ void __launch_bounds__(kBlockThreads) rownorm_block_kernel(const RowA
 
 // ------------------------------------------------------------ dispatch
 template <typename K>
-int resident_ctas(K kernel, size_t smem) {
+int resident_ctas(K kernel, size_t smem, int threads = kThreads) {
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem) != cudaSuccess || n < 1) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) {
     cudaGetLastError();
     n = 1;
   }
   return n;
 }
 
-template <int VPL, int MODE, bool HAS_W>
-cudaError_t launch_warp_on(const RowArgs& a, cudaStream_t s) {
-  cudaError_t err = cudaSuccess;
-  auto kernel = rownorm_warp_kernel<VPL, MODE, HAS_W>;
-  static std::atomic<int> occ{0};  // resident CTAs per SM (smem <= 8 KB never limits it)
+// Resident CTAs per SM of one warp-kernel instantiation (shared memory of at
+// most 8 KB never limits it), cached.
+template <int VPL, int MODE, bool HAS_W, int REGS, int WARPS>
+int warp_occupancy() {
+  static std::atomic<int> occ{0};
   int o = occ.load(std::memory_order_relaxed);
   if (o == 0) {
-    o = resident_ctas(kernel, (size_t)kMaxVpl * 32 * 16);
+    o = resident_ctas(rownorm_warp_kernel<VPL, MODE, HAS_W, REGS, WARPS>, (size_t)kMaxVpl * 32 * 16, 32 * WARPS);
     occ.store(o, std::memory_order_relaxed);
   }
+  return o;
+}
+
+inline int64_t warp_blocks(const RowArgs& a, int max_warps) {
+  const int nw = warps_per_cta(a.rows, max_warps);
+  return (a.rows + nw - 1) / nw;
+}
+
+template <int VPL, int MODE, bool HAS_W, int REGS = rownorm_max_regs<VPL, MODE>(), int WARPS = kWarps>
+cudaError_t launch_warp_on(const RowArgs& a, cudaStream_t s) {
+  cudaError_t err = cudaSuccess;
+  auto kernel = rownorm_warp_kernel<VPL, MODE, HAS_W, REGS, WARPS>;
+  const int o = warp_occupancy<VPL, MODE, HAS_W, REGS, WARPS>();
   const size_t smem = HAS_W ? (size_t)a.nchunks * 16 : 0;
-  const int nw = warps_per_cta(a.rows, kWarps);
-  int64_t blocks = (a.rows + nw - 1) / nw;
+  const int nw = warps_per_cta(a.rows, WARPS);
+  int64_t blocks = warp_blocks(a, WARPS);
   const int64_t wave = (int64_t)device_sm_count() * o;
   if (HRM_RN_WAVES > 0 && blocks > wave * HRM_RN_WAVES) blocks = wave * HRM_RN_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;
@@ -639,7 +676,15 @@ cudaError_t dispatch_vpl(const RowArgs& a, cudaStream_t s) {
   if (need <= 2) return launch_warp_on<2, MODE, HAS_W>(a, s);
   if (need <= 4) return launch_warp_on<4, MODE, HAS_W>(a, s);
   if (need <= 6) return launch_warp_on<6, MODE, HAS_W>(a, s);
-  if (need <= 8) return launch_warp_on<8, MODE, HAS_W>(a, s);
+  if (need <= 8) {
+    if constexpr (MODE == kRms && HRM_RN_NORM8_MAXREGS < HRM_RN_MAXREGS) {
+      // the capped shape only where the launch fits in one wave of it
+      constexpr int kW = HRM_RN_NORM8_WARPS;
+      if (warp_blocks(a, kW) <= (int64_t)device_sm_count() * warp_occupancy<8, MODE, HAS_W, HRM_RN_NORM8_MAXREGS, kW>())
+        return launch_warp_on<8, MODE, HAS_W, HRM_RN_NORM8_MAXREGS, kW>(a, s);
+    }
+    return launch_warp_on<8, MODE, HAS_W>(a, s);
+  }
   return launch_warp_on<16, MODE, HAS_W>(a, s);
 }
 
