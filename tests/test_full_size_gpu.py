@@ -44,6 +44,24 @@ def test_rms_norm_both_paths(oracle, cuda, dtype, rows):
         assert_bits_equal(to_host(y), oracle.rms_norm(x, w, eps=1e-5), f"bf16 {rows} rows")
 
 
+@pytest.mark.parametrize("hidden", [2048, 1600])
+@pytest.mark.parametrize("weighted", [True, False])
+def test_rms_norm_one_wave_shape_boundary(oracle, cuda, hidden, weighted):
+    """Plain bf16 RMSNorm over rows of 1544-2048 elements takes a one-wave shape
+    (64 registers, 8-warp CTAs, 4 CTAs per SM) when the launch fits in one wave
+    of it, and the 80-register 4-warp shape otherwise.  Both sides of the
+    boundary (SMs x 32 rows), and launches with fewer than 8 rows per SM, are
+    bit-exact against the oracle."""
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    edge = sms * 4 * 8
+    rng = np.random.default_rng(hidden + weighted)
+    w = normal_bf16(rng, hidden, 0.1, 1.0) if weighted else None
+    for rows in (edge, edge + 1, edge + 8, sms * 8 - 1, sms + 3):
+        x = normal_bf16(rng, (rows, hidden), 1.5)
+        y = ops.rms_norm(to_dev(x, cuda), to_dev(w, cuda) if weighted else None, eps=1e-5)
+        assert_bits_equal(to_host(y), oracle.rms_norm(x, w, eps=1e-5), f"{rows} x {hidden}")
+
+
 def test_add_rms_norm_16384x2048(oracle, cuda):
     """Fused residual add + RMSNorm bf16 [16384 x 2048], w = 1 + 0.1 N(0,1), eps 1e-5."""
     rng = np.random.default_rng(1)

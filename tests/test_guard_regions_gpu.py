@@ -91,7 +91,7 @@ def test_broadcast(cuda, copies, vec, shift):
 
 # ... plus launches of several waves of CTAs.
 ROW_SHAPES = [(1, 8), (3, 2048), (17, 1536), (5, 200), (2, 6144), (1, 4), (9, 8200), (64, 4096), (1184, 8),
-              (1500, 200), (4096, 2048), (2000, 4096)]
+              (1500, 200), (4096, 2048), (2000, 4096), (4736, 2048), (4737, 1600)]
 
 
 @pytest.mark.parametrize("rows,hidden", ROW_SHAPES)
