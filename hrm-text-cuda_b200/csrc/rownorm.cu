@@ -15,7 +15,8 @@
 // finer grain when a launch ends in a partial wave: RMSNorm [4096 x 2048]
 // 7.22 -> 7.05 us (bf16) and 12.14 -> 11.91 us (fp32) in back-to-back
 // launches, add + RMSNorm [16384 x 2048] 6283 -> 6390 GB/s; 2 and 16 warps
-// were slower.
+// were slower.  A plain bf16 RMSNorm launch that fits in one wave of 8-warp
+// CTAs at 64 registers takes that shape instead (see rownorm_max_regs).
 //
 // Reduction order.  rms_norm_kernel runs 256 threads per row: thread t
 // accumulates x[t], x[t+256], ... with fused multiply-add (src/kernels/
