@@ -106,3 +106,23 @@ def test_reference_arm_at_the_reference_model_dims():
 def test_dims_only_for_chain_and_module():
     res, _ = run_bench("--dims", "hrm-text-1b", "--workload", "swiglu", timeout=300)
     assert res.returncode != 0 and "--dims" in res.stderr
+
+
+def test_reference_arm_under_torchrun_prints_on_rank_zero_only():
+    """Launched as the multi-GPU bench is (torchrun, 2 ranks, 127.0.0.1), rank 0
+    alone runs and prints its line (n_gpus = 2); the other rank exits 0."""
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, OMP_NUM_THREADS="4")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), os.path.join(ROOT, "bench.py"),
+           "--impl", "reference", "--steps", "1", "--warmup", "3", "--tokens", "4096"]
+    res = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = [l for l in res.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, res.stdout[-2000:]
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
