@@ -916,7 +916,8 @@ def reference_checkpoint_arm(args, world):
         "data": "synthetic safetensors file (f32, 0.02 N(0,1) tiled), written once per run",
         "config": checkpoint_config(c.dtype, c.file_bytes, c.pieces, c.bytes_per_step),
         "file_gbs": round(c.file_bytes / sec / 1e9, 3),
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": c.cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": c.cores, "nproc": os.cpu_count(), "kind": "port",
+                         "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -954,7 +955,7 @@ def reference_arm(args, world, rank):
                 "generated on the host by the oracle; the same values as the GPU arm's rank 0",
         "config": chain_config(c.tokens, token_major, world),
         "rows_per_s": round(c.tokens / sec, 1),
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": c.cores, "kind": "port",
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": c.cores, "nproc": os.cpu_count(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -1107,7 +1108,7 @@ def run_ours(args, world, rank, device, peers):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and isinstance(wl, (Chain, LoadCheckpoint)):
         c = wl.cpu_sample()
-        cpu = {"value": round(c["gbs"], 3), "unit": "GB/s", "cores": c["cores"], "kind": "port",
+        cpu = {"value": round(c["gbs"], 3), "unit": "GB/s", "cores": c["cores"], "nproc": os.cpu_count(), "kind": "port",
                "sample": c["sample"]}
 
     collective_point(4)
