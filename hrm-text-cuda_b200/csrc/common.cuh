@@ -45,6 +45,20 @@ __device__ __forceinline__ void st_stream(uint4* p, const uint4& v) { __stcs(p, 
 // Reused read-only data (weights, tables): normal caching.
 __device__ __forceinline__ uint4 ld_keep(const uint4* p) { return __ldg(p); }
 __device__ __forceinline__ float4 ld_keep(const float4* p) { return __ldg(p); }
+// Reused read-only data marked evict-last in L2 (an L2 access policy made by
+// createpolicy), so that streaming traffic is evicted before it.
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint4 ld_keep_last(const uint4* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
 
 // ------------------------------------------- programmatic dependent launch
 // Every kernel calls this before its first global-memory access.  The wait

@@ -234,6 +234,15 @@ constexpr int rownorm_max_regs() {
                       : HRM_RN_MAXREGS;
 }
 
+// Embedding-table rows of embed + RMSNorm loaded evict-last in L2 (1) or with
+// normal caching (0, the default).  Evict-last took the 65536-token embed +
+// RMSNorm from 119-120 to 117 us on B200 (the chain +0.4%), but the table's
+// lines keep that priority after the kernel returns, which would leave less
+// L2 to the GEMMs that follow it in a model; so it is an opt-in build.
+#ifndef HRM_EMB_EVICT_LAST
+#define HRM_EMB_EVICT_LAST 0
+#endif
+
 // L2 prefetch of each warp's first row(s) before the grid dependency wait
 // (1) or none (0).
 #ifndef HRM_RN_PREFETCH
@@ -280,7 +289,11 @@ __global__ void __launch_bounds__(32 * WARPS, min_blocks_for(REGS, 32 * WARPS))
       const int c = lane + 32 * j;
       if (active && c < a.nchunks) {
         if (MODE == kEmbed) {
+#if HRM_EMB_EVICT_LAST
+          v[j] = ld_keep_last(src + c, l2_evict_last_policy());  // table rows may repeat: keep them in L2
+#else
           v[j] = ld_keep(src + c);  // table rows may repeat: keep them in L2
+#endif
         } else {
           v[j] = ld_stream(src + c);
           if (MODE == kAdd) vb[j] = ld_stream(a.b + base + c);
