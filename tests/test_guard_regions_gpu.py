@@ -113,7 +113,8 @@ def test_row_ops(cuda, rows, hidden, shift):
     yf.check("rms_norm f32")
 
 
-@pytest.mark.parametrize("tokens,hidden", [(1, 8), (7, 2048), (300, 1536), (5, 200), (3, 6144)])
+@pytest.mark.parametrize("tokens,hidden", [(1, 8), (7, 2048), (300, 1536), (5, 200), (3, 6144), (64, 1600),
+                                           (148, 2048), (1, 4096)])
 @pytest.mark.parametrize("shift", [0, 1])
 def test_embedding_ops(cuda, tokens, hidden, shift):
     vocab = 100

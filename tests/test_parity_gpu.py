@@ -154,6 +154,18 @@ def test_embedding_bitexact(oracle, rng, cuda, vocab, hidden, tokens, scale):
     assert_bits_equal(to_host(out), oracle.embedding_lookup(ids, table, scale), "embedding")
 
 
+@pytest.mark.parametrize("hidden", [2048, 1536, 1600, 4096, 256])
+@pytest.mark.parametrize("tokens", [1, 3, 8, 64, 148, 300])
+def test_embedding_decode_row_split_bitexact(oracle, rng, cuda, hidden, tokens):
+    """A gather of few tokens splits each row over up to 8 warps (32-chunk
+    blocks p, p + split, ...); every split, including rows whose last block
+    is partial (hidden 1600: 200 chunks), writes each element exactly once."""
+    table = normal_bf16(rng, (3000, hidden), 0.02)
+    ids = rng.integers(0, 3000, tokens, dtype=np.uint32)
+    out = ops.embedding_lookup(to_dev(ids, cuda), to_dev(table, cuda), 45.254834)
+    assert_bits_equal(to_host(out), oracle.embedding_lookup(ids, table, 45.254834), f"{tokens} x {hidden}")
+
+
 def test_embedding_misaligned_table(oracle, rng, cuda):
     table = normal_bf16(rng, (40, 64), 0.02)
     ids = rng.integers(0, 40, 21, dtype=np.uint32)
