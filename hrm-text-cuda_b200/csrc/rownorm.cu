@@ -16,7 +16,8 @@
 // 7.22 -> 7.05 us (bf16) and 12.14 -> 11.91 us (fp32) in back-to-back
 // launches, add + RMSNorm [16384 x 2048] 6283 -> 6390 GB/s; 2 and 16 warps
 // were slower.  A plain bf16 RMSNorm launch that fits in one wave of 8-warp
-// CTAs at 64 registers takes that shape instead (see rownorm_max_regs).
+// CTAs at 64 registers takes that shape instead (see rownorm_max_regs), and a
+// decode-size launch of wide rows gives each row a CTA (rownorm_cta_kernel).
 //
 // Reduction order.  rms_norm_kernel runs 256 threads per row: thread t
 // accumulates x[t], x[t+256], ... with fused multiply-add (src/kernels/
@@ -328,6 +329,77 @@ __global__ void __launch_bounds__(32 * WARPS, min_blocks_for(REGS, 32 * WARPS))
         st_stream(a.y + base + c, norm8<HAS_W>(v[j], inv, wv));
       }
     }
+  }
+}
+
+// ------------------------------------------------- bf16 decode-size path
+// A launch of at most HRM_RN_CTA_ROWS_PER_SM rows per SM gives each row a CTA
+// of nchunks / 32 warps (up to 16): thread c moves the row's 16-byte chunk c
+// (the chunk lane c % 32 of the warp kernel holds as its chunk j = c / 32), so
+// the loads, the add / scale, the stores and the normalisation of a row spread
+// over its warps instead of running one after another in one warp.  The row's
+// chunks go to shared memory, and warp 0 replays the warp kernel's summation
+// from there -- chunk j = 0, 1, ... per lane, then ref_tree_bf16 -- so the sum
+// of squares, and every output, stay bit-identical.  Each thread reads its own
+// chunk before writing any output of it (in place use stays safe), and the
+// weight chunk comes straight from global memory (L2).
+#ifndef HRM_RN_CTA_ROWS_PER_SM
+#define HRM_RN_CTA_ROWS_PER_SM 1
+#endif
+// ... for rows of more than HRM_RN_CTA_MIN_CHUNKS 16-byte chunks: at 6 chunks
+// per lane (1536 bf16) the warp kernel is as fast (64 rows of add + RMSNorm:
+// 1.93 us, against 1.97 us in CTAs of 6 warps; at 2048 bf16 2.22 -> 2.08 us).
+#ifndef HRM_RN_CTA_MIN_CHUNKS
+#define HRM_RN_CTA_MIN_CHUNKS 193
+#endif
+constexpr int kCtaMaxThreads = kMaxVpl * 32;  // 512: a row of 4096 bf16
+
+template <int MODE, bool HAS_W>
+__global__ void __launch_bounds__(kCtaMaxThreads) rownorm_cta_kernel(const RowArgs a) {
+  if (HRM_RN_PREFETCH && MODE != kEmbed && threadIdx.x == 0 && (int64_t)blockIdx.x < a.rows) {
+    prefetch_l2(a.x + (int64_t)blockIdx.x * a.nchunks, (uint32_t)a.nchunks * 16u);
+    if (MODE == kAdd) prefetch_l2(a.b + (int64_t)blockIdx.x * a.nchunks, (uint32_t)a.nchunks * 16u);
+  }
+  grid_dependency_begin();
+  __shared__ uint4 s_row[kCtaMaxThreads];
+  __shared__ float s_inv;
+  const int c = threadIdx.x, lane = c & 31;
+  const bool has = c < a.nchunks;
+  uint4 wv = make_uint4(0, 0, 0, 0);
+  if (HAS_W && has) wv = ld_keep(a.w + c);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.nchunks;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (has) {
+      if (MODE == kEmbed) {
+        uint32_t id = a.ids[row];
+        if (id >= a.vocab) id = a.vocab - 1;  // src/kernels/embedding_lookup.cu:35
+        v = scale8(ld_keep(a.x + (int64_t)id * a.nchunks + c), a.scale);
+        if (a.r != nullptr) st_stream(a.r + base + c, v);
+      } else {
+        v = ld_stream(a.x + base + c);
+        if (MODE == kAdd) {
+          v = add8(v, ld_stream(a.b + base + c));
+          st_stream(a.r + base + c, v);
+        }
+      }
+      s_row[c] = v;
+    }
+    __syncthreads();
+    if (c < 32) {
+      float p[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) p[e] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kMaxVpl; ++j) {
+        if (lane + 32 * j < a.nchunks) accum8(p, s_row[lane + 32 * j]);
+      }
+      const float inv = inv_rms(ref_tree_bf16(p), a.hidden, a.eps);
+      if (lane == 0) s_inv = inv;
+    }
+    __syncthreads();
+    if (has) st_stream(a.y + base + c, norm8<HAS_W>(v, s_inv, wv));
+    __syncthreads();  // s_row and s_inv are rewritten by the next row
   }
 }
 
@@ -804,6 +876,12 @@ cudaError_t launch_bf16_rows(const void* x, const void* b, const uint32_t* ids, 
     a.vocab = (uint32_t)vocab;
     a.scale = scale;
     a.eps = eps;
+    if (HRM_RN_CTA_ROWS_PER_SM > 0 && a.nchunks >= HRM_RN_CTA_MIN_CHUNKS &&
+        rows <= (int64_t)device_sm_count() * HRM_RN_CTA_ROWS_PER_SM) {
+      const int threads = (a.nchunks + 31) / 32 * 32;
+      return w ? launch_kernel(rownorm_cta_kernel<MODE, true>, rows, threads, 0, s, a)
+               : launch_kernel(rownorm_cta_kernel<MODE, false>, rows, threads, 0, s, a);
+    }
 #if HRM_RN_BULK
     size_t smem = 0;
     const int nwarps = bulk_plan(a.nchunks, MODE == kAdd ? 2 : 1, w != nullptr, &smem);

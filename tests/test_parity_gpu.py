@@ -130,6 +130,34 @@ def test_add_rms_norm_bitexact(oracle, rng, cuda, rows, hidden, with_weight):
     assert_bits_equal(to_host(y), wy, "normed")
 
 
+@pytest.mark.parametrize("hidden", [1536, 1544, 2048, 4096])
+@pytest.mark.parametrize("weighted", [False, True])
+def test_row_ops_decode_size_paths(oracle, rng, cuda, hidden, weighted):
+    """Launches of at most one row per SM over rows of more than 192 chunks
+    give each row a CTA of one warp per 32 chunks (warp 0 replays the
+    summation from shared memory); narrower rows, and one row more than the
+    SM count, keep the warp kernel.  Every op, both sides of both boundaries,
+    bit-exact against the oracle."""
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    w = normal_bf16(rng, hidden, 0.1, 1.0) if weighted else None
+    dw = None if w is None else to_dev(w, cuda)
+    table = normal_bf16(rng, (700, hidden), 0.02)
+    for rows in (1, 64, sms, sms + 1):
+        x, b = normal_bf16(rng, (rows, hidden), 1.5), normal_bf16(rng, (rows, hidden))
+        y = ops.rms_norm(to_dev(x, cuda), dw, eps=1e-5)
+        assert_bits_equal(to_host(y), oracle.rms_norm(x, w, eps=1e-5), f"rms_norm {rows} x {hidden}")
+        dx = to_dev(x, cuda)
+        r, y = ops.add_rms_norm(dx, to_dev(b, cuda), dw, eps=1e-5, residual_out=dx)  # in place, as the layer loop
+        wr, wy = oracle.add_rms_norm(x, b, w, eps=1e-5)
+        assert_bits_equal(to_host(r), wr, f"add_rms_norm residual {rows} x {hidden}")
+        assert_bits_equal(to_host(y), wy, f"add_rms_norm normed {rows} x {hidden}")
+        ids = rng.integers(0, 705, rows, dtype=np.uint32)  # a few out of range: clamped
+        h, y = ops.embed_rms_norm(to_dev(ids, cuda), to_dev(table, cuda), 45.254834, dw, eps=1e-5, keep_hidden=True)
+        wh, wy = oracle.embed_rms_norm(ids, table, 45.254834, w, eps=1e-5)
+        assert_bits_equal(to_host(h), wh, f"embed_rms_norm hidden {rows} x {hidden}")
+        assert_bits_equal(to_host(y), wy, f"embed_rms_norm normed {rows} x {hidden}")
+
+
 def test_add_rms_norm_residual_in_place(oracle, rng, cuda):
     x, b = normal_bf16(rng, (40, 2048)), normal_bf16(rng, (40, 2048))
     wr, wy = oracle.add_rms_norm(x, b, None, eps=1e-6)
