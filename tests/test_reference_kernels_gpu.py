@@ -298,7 +298,8 @@ def test_throughput_vs_reference_kernels(ref_sm100a, cuda):
     del sc, bufs
     out = {k: {"ours_gbs": round(a / 1e6, 1), "reference_gbs": round(b_ / 1e6, 1), "speedup": round(a / b_, 2)}
            for k, (a, b_) in res.items()}
-    # decode shapes: latency per call (us), 8 calls per CUDA graph
+    # decode shapes: latency per call (us), 50 calls per CUDA graph (a graph's
+    # launch, about 4 us, spread over its calls)
     dq, dk = rn((8, 16, 1, 128)), rn((8, 16, 1, 128))
     ids64 = ids[:64].contiguous()
     e64 = torch.empty((64, 2048), dtype=bf, device=cuda)
@@ -317,8 +318,28 @@ def test_throughput_vs_reference_kernels(ref_sm100a, cuda):
                                         lambda: (ref.additive_inject(x64, b64, r64), ref.rms_norm(r64, y64, 1e-5))),
         "swiglu_decode_64x5632": (lambda: ops.swiglu_ffn(g64, u64, out=o64), lambda: ref.swiglu_ffn(g64, u64, o64)),
     }
+    # the decode chain on 64 tokens: embed + RMSNorm -> RoPE -> add + RMSNorm ->
+    # SwiGLU (4 launches) against the reference's embedding_lookup -> rms_norm ->
+    # rope_embed -> additive_inject -> rms_norm -> swiglu_ffn (6 launches)
+    cq, ck = rn((64, 16, 1, 128)), rn((64, 16, 1, 128))
+    h64, n64 = torch.empty_like(x64), torch.empty_like(x64)
+
+    def chain_ours():
+        ops.embed_rms_norm(ids64, tab, 45.254834, None, 1e-5, hidden_out=h64, normed_out=n64)
+        ops.rope_embed(cq, ck, 4095, 10000.0, tab4096)
+        ops.add_rms_norm(x64, h64, None, 1e-5, residual_out=r64, normed_out=y64)
+        ops.swiglu_ffn(g64, u64, out=o64)
+
+    def chain_reference():
+        ref.embedding_lookup(ids64, tab, h64, 45.254834)
+        ref.rms_norm(h64, n64, 1e-5)
+        ref.rope_embed(cq, ck, 4095, 10000.0)
+        ref.additive_inject(x64, h64, r64)
+        ref.rms_norm(r64, y64, 1e-5)
+        ref.swiglu_ffn(g64, u64, o64)
+    dec["chain_decode_64_tokens"] = (chain_ours, chain_reference)
     for k, (ours, theirs) in dec.items():
-        a_us, b_us = _time_graph([ours] * 8) * 1e3, _time_graph([theirs] * 8) * 1e3
+        a_us, b_us = _time_graph([ours] * 50, replays=20) * 1e3, _time_graph([theirs] * 50, replays=20) * 1e3
         out[k] = {"ours_us": round(a_us, 2), "reference_us": round(b_us, 2), "speedup": round(b_us / a_us, 2)}
     print(json.dumps({"vs_reference_kernels": out}))
     path = os.environ.get("HRM_REF_TIMING_OUT")
