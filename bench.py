@@ -436,6 +436,146 @@ class CpuChain:
         lib.ora_swiglu_ffn(p["g"], p["u"], p["y"], T * INTER)
 
 
+def single_op_spec(name):
+    """(config, algorithmic bytes per step, rows per step) of a single-op workload;
+    shared by both arms, so that they report the same config and bytes."""
+    if name == "add_rms_norm":        # [16384 x 2048] bf16, weight, eps 1e-5
+        return {"workload": "fused residual add + RMSNorm bf16 [16384 x 2048]", "rows": 16384}, 16384 * HIDDEN * 8, 16384
+    if name == "rms_norm_f32":        # [4096 x 2048] fp32, weight, eps 1e-5
+        return {"workload": "RMSNorm fp32 [4096 x 2048]", "rows": 4096}, 4096 * HIDDEN * 8, 4096
+    if name == "rms_norm":            # [4096 x 2048] bf16, weight, eps 1e-5
+        return {"workload": "RMSNorm bf16 [4096 x 2048]", "rows": 4096}, 4096 * HIDDEN * 4, 4096
+    if name == "rope":                # Q, K [8, 16, 4096, 128], table
+        return ({"workload": "RoPE Q/K [8, 16, 4096, 128] bf16, fp32 table", "tokens": 8 * 4096},
+                4 * 2 * 8 * HEADS * 4096 * HEAD_DIM, 8 * 4096)
+    if name == "swiglu":              # gate, up [32768 x 5632]
+        return {"workload": "SwiGLU bf16 [32768 x 5632]", "rows": 32768}, 32768 * INTER * 6, 32768
+    if name == "embedding":           # table [32000 x 2048], 65536 ids
+        return ({"workload": "embedding gather [32000 x 2048] table, 65536 ids", "tokens": 65536},
+                65536 * (4 + 2 * 2 * HIDDEN), 65536)
+    if name == "split_rope":          # gqkv [16, 4096, 4 x 16 x 128] -> gate, q, k, v + KV cache, table
+        T = 16 * 4096
+        return ({"workload": "split_gqkv + RoPE + KV-cache write, gqkv [16, 4096, 4 x 16 x 128] bf16", "tokens": T},
+                T * (4 + 4 + 2) * HEADS * HEAD_DIM * 2, T)
+    if name == "attn_gate":           # attn [65536 x 2048] *= sigmoid(gate), in place
+        return {"workload": "attention gate in place [65536 x 2048] bf16", "rows": 65536}, 65536 * HIDDEN * 6, 65536
+    if name == "convert_f32":         # 2^28 f32 checkpoint values -> bf16 (a 1 GB tensor)
+        n = 1 << 28
+        return {"workload": "checkpoint f32 -> bf16 conversion, 2^28 values", "elements": n}, n * 6, n
+    raise ValueError(name)
+
+
+def single_op_sets(bytes_per_step):
+    """Input sets the GPU arm rotates so that their total exceeds 3x L2."""
+    return max(1, -(-3 * L2_BYTES // bytes_per_step))
+
+
+def single_op_l2_note(bytes_per_step):
+    nbuf = single_op_sets(bytes_per_step)
+    return (f"{nbuf} rotating input sets ({nbuf * bytes_per_step / 1e6:.0f} MB > 3x L2)"
+            if nbuf > 1 else "inputs larger than L2; no flush")
+
+
+class CpuSingleOp:
+    """A single-op workload on the host cores through the oracle (a C
+    restatement of the reference's kernels, all OpenMP threads): the GPU arm's
+    shapes and byte count, seeded host inputs of the same distributions,
+    outputs allocated once, in place where the reference's kernel is.  For
+    split_rope it runs the reference's three steps (split_gqkv, rope_embed,
+    kv_cache_update).  Imports nothing of the library."""
+
+    def __init__(self, name):
+        import ctypes
+
+        import numpy as np
+
+        sys.path.insert(0, ROOT)
+        from oracle import Oracle
+
+        self.name = name
+        self.config, self.bytes, self.rows = single_op_spec(name)
+        self.o = o = Oracle()
+        o.set_threads(len(os.sched_getaffinity(0)))
+        self.cores = o.max_threads()
+        u16 = np.uint16
+        tag = iter(range(1, 100))
+
+        def nb(shape, std=1.0, mean=0.0):
+            return o.fill_normal_bf16(np.empty(shape, u16), SEED + 7, next(tag), 0, std, mean)
+
+        p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+        lib = o.lib
+        if name in ("rms_norm", "add_rms_norm"):
+            R = self.rows
+            x, w, y = nb((R, HIDDEN)), nb(HIDDEN, 0.1, 1.0), np.empty((R, HIDDEN), u16)
+            if name == "rms_norm":
+                self.run_once = lambda: lib.ora_rms_norm(p(x), p(y), p(w), R, HIDDEN, EPS)
+            else:
+                b, r = nb((R, HIDDEN)), np.empty((R, HIDDEN), u16)
+                self.run_once = lambda: lib.ora_add_rms_norm(p(x), p(b), p(r), p(y), p(w), R, HIDDEN, EPS)
+            self._keep = [x, w, y] + ([b, r] if name == "add_rms_norm" else [])
+        elif name == "rms_norm_f32":
+            rng = np.random.default_rng(SEED + 7)
+            x = rng.standard_normal((4096, HIDDEN), dtype=np.float32)
+            w = (1 + 0.1 * rng.standard_normal(HIDDEN, dtype=np.float32)).astype(np.float32)
+            y = np.empty_like(x)
+            self.run_once = lambda: lib.ora_rms_norm_f32(p(x), p(y), p(w), 4096, HIDDEN, EPS)
+            self._keep = [x, w, y]
+        elif name == "rope":
+            q, k, tab = nb((8, HEADS, 4096, HEAD_DIM)), nb((8, HEADS, 4096, HEAD_DIM)), o.rope_table(4096, HEAD_DIM, THETA)
+            self.run_once = lambda: lib.ora_rope_embed(p(q), p(k), 8, HEADS, 4096, HEAD_DIM, 0, THETA, p(tab))
+            self._keep = [q, k, tab]
+        elif name == "swiglu":
+            g, u, y = nb((32768, INTER), 0.5), nb((32768, INTER), 0.5), np.empty((32768, INTER), u16)
+            self.run_once = lambda: lib.ora_swiglu_ffn(p(g), p(u), p(y), 32768 * INTER)
+            self._keep = [g, u, y]
+        elif name == "embedding":
+            tab, y = nb((VOCAB, HIDDEN), 0.02), np.empty((65536, HIDDEN), u16)
+            ids = o.fill_ids(np.empty(65536, np.uint32), SEED + 7, next(tag), VOCAB)
+            self.run_once = lambda: lib.ora_embedding_lookup(p(ids), p(tab), p(y), 65536, HIDDEN, VOCAB, SCALE)
+            self._keep = [tab, y, ids]
+        elif name == "attn_gate":
+            g, a = nb((65536, HIDDEN)), nb((65536, HIDDEN))
+            self.run_once = lambda: lib.ora_gated_attn_output(p(g), p(a), p(a), 65536 * HIDDEN)
+            self._keep = [g, a]
+        elif name == "convert_f32":
+            n = self.rows
+            src = np.random.default_rng(SEED + 7).standard_normal(n, dtype=np.float32)
+            y = np.empty(n, u16)
+            self.run_once = lambda: lib.ora_convert_to_bf16(p(src), 1, p(y), n)  # 1: f32
+            self._keep = [src, y]
+        elif name == "split_rope":
+            B, S = 16, 4096
+            gq = nb((B, S, 4 * HEADS * HEAD_DIM))
+            gate = np.empty((B, S, HEADS, HEAD_DIM), u16)
+            q, k, v, kc, vc = (np.empty((B, HEADS, S, HEAD_DIM), u16) for _ in range(5))
+            tab = o.rope_table(S, HEAD_DIM, THETA)
+
+            def run():
+                lib.ora_split_gqkv(p(gq), p(gate), p(q), p(k), p(v), B, S, HEADS, HEAD_DIM)
+                lib.ora_rope_embed(p(q), p(k), B, HEADS, S, HEAD_DIM, 0, THETA, p(tab))
+                lib.ora_kv_cache_update(p(k), p(v), p(kc), p(vc), B, HEADS, S, HEAD_DIM, S, 0, 0)
+            self.run_once = run
+            self._keep = [gq, gate, q, k, v, kc, vc, tab]
+        else:
+            raise ValueError(name)
+
+    def sample(self, min_seconds=5.0, max_reps=50):
+        """GB/s over a bounded number of whole steps (at least min_seconds)."""
+        self.run_once()  # first touch of the outputs
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            self.run_once()
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= min_seconds or reps >= max_reps:
+                break
+        sec = el / reps
+        return {"gbs": self.bytes / sec / 1e9, "sec_per_sample": sec, "cores": self.cores,
+                "sample": f"{reps} whole steps of the {self.config['workload']} workload, oracle with "
+                          f"{self.cores} OpenMP threads"}
+
+
 class SingleOp:
     """One of the per-op workloads (the other layer-op configurations)."""
 
@@ -447,79 +587,60 @@ class SingleOp:
         self.torch, self.ops, self.device, self.name = torch, ops, device, name
         gen = torch.Generator(device=device).manual_seed(2000 + rank)
         bf = torch.bfloat16
+        self.cfg, self.bytes_per_step, self.rows_per_step = single_op_spec(name)
         if name == "add_rms_norm":        # [16384 x 2048] bf16, weight, eps 1e-5
             R = 16384
             self.w = randn_bf16(HIDDEN, gen, device, 0.1, 1.0)
-            self.bytes_per_step, self.rows_per_step = R * HIDDEN * 8, R
             mk = lambda: (randn_bf16((R, HIDDEN), gen, device), randn_bf16((R, HIDDEN), gen, device),
                           torch.empty((R, HIDDEN), dtype=bf, device=device),
                           torch.empty((R, HIDDEN), dtype=bf, device=device))
-            self.cfg = {"workload": "fused residual add + RMSNorm bf16 [16384 x 2048]", "rows": R}
         elif name == "rms_norm_f32":      # [4096 x 2048] fp32, weight, eps 1e-5
             R = 4096
             self.w = torch.randn(HIDDEN, generator=gen, device=device) * 0.1 + 1
-            self.bytes_per_step, self.rows_per_step = R * HIDDEN * 8, R
             mk = lambda: (torch.randn((R, HIDDEN), generator=gen, device=device),
                           torch.empty((R, HIDDEN), device=device))
-            self.cfg = {"workload": "RMSNorm fp32 [4096 x 2048]", "rows": R}
         elif name == "rms_norm":          # [4096 x 2048] bf16, weight, eps 1e-5
             R = 4096
             self.w = randn_bf16(HIDDEN, gen, device, 0.1, 1.0)
-            self.bytes_per_step, self.rows_per_step = R * HIDDEN * 4, R
             mk = lambda: (randn_bf16((R, HIDDEN), gen, device), torch.empty((R, HIDDEN), dtype=bf, device=device))
-            self.cfg = {"workload": "RMSNorm bf16 [4096 x 2048]", "rows": R}
         elif name == "rope":              # Q, K [8, 16, 4096, 128], table
             shape = (8, HEADS, 4096, HEAD_DIM)
             self.table = ops.rope_table(4096, HEAD_DIM, THETA, device)
-            self.bytes_per_step, self.rows_per_step = 4 * 2 * 8 * HEADS * 4096 * HEAD_DIM, 8 * 4096
             mk = lambda: (randn_bf16(shape, gen, device), randn_bf16(shape, gen, device))
-            self.cfg = {"workload": "RoPE Q/K [8, 16, 4096, 128] bf16, fp32 table", "tokens": 8 * 4096}
         elif name == "swiglu":            # gate, up [32768 x 5632]
             shape = (32768, INTER)
-            self.bytes_per_step, self.rows_per_step = 32768 * INTER * 6, 32768
             mk = lambda: (randn_bf16(shape, gen, device, 0.5), randn_bf16(shape, gen, device, 0.5),
                           torch.empty(shape, dtype=bf, device=device))
-            self.cfg = {"workload": "SwiGLU bf16 [32768 x 5632]", "rows": 32768}
         elif name == "embedding":         # table [32000 x 2048], 65536 ids
             T = 65536
             self.tab = randn_bf16((VOCAB, HIDDEN), gen, device, 0.02)
-            self.bytes_per_step, self.rows_per_step = T * (4 + 2 * 2 * HIDDEN), T
             mk = lambda: (torch.randint(0, VOCAB, (T,), generator=gen, device=device, dtype=torch.int32),
                           torch.empty((T, HIDDEN), dtype=bf, device=device))
-            self.cfg = {"workload": "embedding gather [32000 x 2048] table, 65536 ids", "tokens": T}
         elif name == "split_rope":        # gqkv [16, 4096, 4 x 16 x 128] -> gate, q, k, v + KV cache, table
             B, S = 16, 4096
             T = B * S
             self.table = ops.rope_table(S, HEAD_DIM, THETA, device)
-            self.bytes_per_step, self.rows_per_step = T * (4 + 4 + 2) * HEADS * HEAD_DIM * 2, T
             mk = lambda: (randn_bf16((B, S, 4 * HEADS * HEAD_DIM), gen, device),
                           torch.empty((B, S, HEADS, HEAD_DIM), dtype=bf, device=device),
                           *(torch.empty((B, HEADS, S, HEAD_DIM), dtype=bf, device=device) for _ in range(5)))
-            self.cfg = {"workload": "split_gqkv + RoPE + KV-cache write, gqkv [16, 4096, 4 x 16 x 128] bf16",
-                        "tokens": T}
         elif name == "attn_gate":         # attn [65536 x 2048] *= sigmoid(gate), in place
             shape = (65536, HIDDEN)
-            self.bytes_per_step, self.rows_per_step = 65536 * HIDDEN * 6, 65536
             mk = lambda: (randn_bf16(shape, gen, device), randn_bf16(shape, gen, device))
-            self.cfg = {"workload": "attention gate in place [65536 x 2048] bf16", "rows": 65536}
         elif name == "convert_f32":       # 2^28 f32 checkpoint values -> bf16 (a 1 GB tensor)
             n = 1 << 28
-            self.bytes_per_step, self.rows_per_step = n * 6, n
             mk = lambda: (torch.randn(n, generator=gen, device=device).view(torch.uint8),
                           torch.empty(n, dtype=bf, device=device))
-            self.cfg = {"workload": "checkpoint f32 -> bf16 conversion, 2^28 values", "elements": n}
         else:
             raise ValueError(name)
         # Rotate input sets so that their total exceeds 3x L2: no step finds its inputs in L2.
-        nbuf = max(1, -(-3 * L2_BYTES // self.bytes_per_step))
+        nbuf = single_op_sets(self.bytes_per_step)
         self.bufs = [mk() for _ in range(nbuf)]
         self.i = 0
         self.kernels = [name]
         self.dominant = name
         self.kernel_bytes = {name: self.bytes_per_step}
         self.footprint = self.bytes_per_step
-        self.cfg["l2"] = (f"{nbuf} rotating input sets ({nbuf * self.bytes_per_step / 1e6:.0f} MB > 3x L2)"
-                          if nbuf > 1 else "inputs larger than L2; no flush")
+        self.cfg["l2"] = single_op_l2_note(self.bytes_per_step)
         self.config = self.cfg
 
     def step(self, stream=None, events=None):
@@ -577,7 +698,8 @@ class SingleOp:
         return t0.elapsed_time(t1) / steps, h2d, d2h, launches
 
     def cpu_sample(self, min_seconds=5.0):
-        return None
+        """The oracle on the same workload's shapes (CpuSingleOp), a bounded sample."""
+        return CpuSingleOp(self.name).sample(min_seconds)
 
 
 # The reference model's shapes (HrmConfig defaults, src/lib.rs:40-60).
@@ -932,6 +1054,37 @@ def reference_checkpoint_arm(args, world):
     print(json.dumps(line), flush=True)
 
 
+SINGLE_OPS = ("add_rms_norm", "rms_norm_f32", "rms_norm", "rope", "swiglu", "embedding", "split_rope", "attn_gate",
+              "convert_f32")
+
+
+def reference_single_op_arm(args, world):
+    """A single-op workload's reference path on the host cores: the oracle (all
+    threads) over whole steps of the GPU arm's shapes, with its config and bytes."""
+    c = CpuSingleOp(args.workload)
+    for _ in range(args.warmup):
+        c.run_once()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        c.run_once()
+    sec = (time.perf_counter() - t0) / args.steps
+    gbs = c.bytes / sec / 1e9
+    sample = f"whole steps of the {c.config['workload']} workload, oracle with {c.cores} OpenMP threads"
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1000, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32" if args.workload == "rms_norm_f32" else "bf16 (fp32 math)",
+        "data": "synthetic, seeded, generated on the host by the oracle",
+        "config": dict(c.config, l2=single_op_l2_note(c.bytes), parallelism=f"{world} row shards, no collective"),
+        "rows_per_s": round(c.rows / sec, 1),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": c.cores, "nproc": os.cpu_count(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def reference_arm(args, world, rank):
     """The reference's path on the host cores: the oracle, all threads, over the
     whole pass of the GPU arm's workload (rank 0's shard of --tokens tokens).
@@ -941,9 +1094,12 @@ def reference_arm(args, world, rank):
     if args.workload == "load_checkpoint":
         reference_checkpoint_arm(args, world)
         return
+    if args.workload in SINGLE_OPS:
+        reference_single_op_arm(args, world)
+        return
     if args.workload != "chain":
-        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the chain and "
-                                                                "load_checkpoint workloads"}))
+        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the chain, the "
+                                                                "single-op and load_checkpoint workloads"}))
         return
     token_major = args.qk_layout == "token"
     c = CpuChain(args.tokens, token_major)
@@ -1115,7 +1271,7 @@ def run_ours(args, world, rank, device, peers):
         if isinstance(wl, LoadCheckpoint):
             e2e["file_gbs"] = round(wl.file_gbs, 3)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu and isinstance(wl, (Chain, LoadCheckpoint)):
+    if rank == 0 and world == 1 and not args.no_cpu and isinstance(wl, (Chain, LoadCheckpoint, SingleOp)):
         c = wl.cpu_sample()
         cpu = {"value": round(c["gbs"], 3), "unit": "GB/s", "cores": c["cores"], "nproc": os.cpu_count(), "kind": "port",
                "sample": c["sample"]}
@@ -1136,7 +1292,8 @@ def run_ours(args, world, rank, device, peers):
     line = {
         "metric": METRIC, "value": round(value_gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 (fp32 math)", "data": getattr(wl, "data", "synthetic (seeded, generated on device)"),
+        "vs_baseline": None, "dtype": "fp32" if wl.name == "rms_norm_f32" else "bf16 (fp32 math)",
+        "data": getattr(wl, "data", "synthetic (seeded, generated on device)"),
         "config": wl.config if isinstance(wl, Chain) else dict(wl.config, parallelism=f"{world} row shards, no collective"),
         "pct_of_peak": round(100 * value_gbs / (world * peak), 2), "rows_per_s": round(rows_per_s, 1),
         "effective_gbs": round(world * wl.footprint / (ms_step / 1e3) / 1e9, 3),

@@ -13,6 +13,8 @@ import os
 import subprocess
 import sys
 
+import pytest
+
 from conftest import ROOT
 
 
@@ -56,10 +58,11 @@ def test_reference_arm_defaults_to_the_whole_gpu_workload():
     assert cfg["tokens_per_gpu"] == 65536 and cfg["qk_shape"] == [16, 4096, 16, 128]
 
 
-def test_reference_arm_loads_nothing_of_the_library():
+@pytest.mark.parametrize("workload", [["--tokens", "4096"], ["--workload", "rms_norm_f32"]])
+def test_reference_arm_loads_nothing_of_the_library(workload):
     code = (
         "import sys, runpy\n"
-        "sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '3', '--tokens', '4096']\n"
+        f"sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '3', *{workload!r}]\n"
         "runpy.run_path('bench.py', run_name='__main__')\n"
         "maps = open('/proc/self/maps').read()\n"
         "print('LOADED', [m for m in sys.modules if m.startswith('hrm_layer_ops')], 'libhrm_ops' in maps,"
@@ -83,11 +86,28 @@ def test_bench_byte_counts_equal_the_library_s():
 
 
 def test_reference_arm_other_workload_is_unavailable():
-    res, lines = run_bench("--impl", "reference", "--workload", "swiglu", "--steps", "1", "--warmup", "3")
+    res, lines = run_bench("--impl", "reference", "--workload", "module", "--steps", "1", "--warmup", "3")
     assert res.returncode == 0, res.stderr[-2000:]
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["unavailable"]
+
+
+def test_reference_arm_single_op_workload():
+    """The CPU-runnable configuration (RMSNorm fp32 [4096 x 2048] + weight) through
+    the oracle: one line with the GPU arm's config and byte count."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    res, lines = run_bench("--impl", "reference", "--workload", "rms_norm_f32", "--steps", "2", "--warmup", "3")
+    assert res.returncode == 0, res.stderr[-2000:]
+    assert len(lines) == 1, res.stdout[-2000:]
+    d = json.loads(lines[0])
+    cfg, nbytes, rows = bench.single_op_spec("rms_norm_f32")
+    assert d["impl"] == "reference" and d["value"] > 0 and d["dtype"] == "fp32"
+    assert d["config"] == dict(cfg, l2=bench.single_op_l2_note(nbytes), parallelism="1 row shards, no collective")
+    assert abs(d["rows_per_s"] * d["ms_per_step"] / 1e3 - rows) < 1 + 1e-3 * rows
+    assert abs(d["value"] * d["ms_per_step"] * 1e6 - nbytes) < 1e-3 * nbytes
 
 
 def test_warmup_below_three_is_refused():
