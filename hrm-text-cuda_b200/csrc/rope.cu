@@ -148,27 +148,50 @@ __device__ __forceinline__ void shared_cos_sin(const float* s_cos, const float* 
   sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
 }
 
+// First position of a tile and its batch index (32-bit: tile counts fit 31 bits).
+template <typename Args>
+__device__ __forceinline__ int64_t tile_first_pos(const Args& a, int tile, int& bi) {
+  bi = tile / a.tiles_per_batch;
+  return (int64_t)(tile - bi * a.tiles_per_batch) * a.pt;
+}
+
+// In-kernel angles of the CTA's first tile, evaluated before the grid
+// dependency wait: they depend on the launch arguments only (positions,
+// offset, theta), so their expf / logf / sincosf latency overlaps the previous
+// kernel's drain instead of preceding this kernel's loads.  Published by the
+// barrier at the top of the first tile.
+template <typename Args>
+__device__ __forceinline__ void first_tile_angles(const Args& a, float* s_cos, float* s_sin) {
+  if ((int)blockIdx.x >= a.ntiles) return;
+  int bi;
+  const int64_t s_base = tile_first_pos(a, (int)blockIdx.x, bi);
+  tile_angles(s_cos, s_sin, s_base, a.seq, a.pt, a.lg + 3, a.offset, a.head_dim, a.theta);
+}
+
 // Thread layout within a tile (g, ht powers of two): lane j of its row, head
 // slice, position in the tile.  Shifts and masks, and 32-bit tile arithmetic:
 // at decode sizes a launch is a handful of CTAs whose time is latency, where a
 // 64-bit division costs a visible fraction.
 template <bool TABLE>
 __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) rope_tile_kernel(const RopeArgs a) {
+  __shared__ __align__(16) float s_cos[TABLE ? 1 : kMaxAngles], s_sin[TABLE ? 1 : kMaxAngles];
+  if (!TABLE) first_tile_angles(a, s_cos, s_sin);
   grid_dependency_begin();
   const int j = threadIdx.x & (a.g - 1);
   const int rest = threadIdx.x >> a.lg;
   const int slice = rest & (a.ht - 1);
   const int pl = rest >> a.lht;
 
-  __shared__ __align__(16) float s_cos[TABLE ? 1 : kMaxAngles], s_sin[TABLE ? 1 : kMaxAngles];
   for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
-    const int bi = tile / a.tiles_per_batch;
+    int bi;
+    const int64_t s_base = tile_first_pos(a, tile, bi);
     const int64_t b = bi;
-    const int64_t s_base = (int64_t)(tile - bi * a.tiles_per_batch) * a.pt;
     const int64_t s = s_base + pl;
     if (!TABLE) {
-      __syncthreads();  // the previous tile's angles are no longer read
-      tile_angles(s_cos, s_sin, s_base, a.seq, a.pt, a.lg + 3, a.offset, a.head_dim, a.theta);
+      if (tile != (int)blockIdx.x) {
+        __syncthreads();  // the previous tile's angles are no longer read
+        tile_angles(s_cos, s_sin, s_base, a.seq, a.pt, a.lg + 3, a.offset, a.head_dim, a.theta);
+      }
       __syncthreads();
     }
     if (s >= a.seq) continue;
@@ -297,6 +320,8 @@ struct SplitArgs {
 
 template <bool TABLE, bool CACHE>
 __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) split_rope_tile_kernel(const SplitArgs a) {
+  __shared__ __align__(16) float s_cos[TABLE ? 1 : kMaxAngles], s_sin[TABLE ? 1 : kMaxAngles];
+  if (!TABLE) first_tile_angles(a, s_cos, s_sin);
   grid_dependency_begin();
   const int j = threadIdx.x & (a.g - 1);
   const int rest = threadIdx.x >> a.lg;
@@ -305,15 +330,16 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) split_rope_tile_
   const int row_chunks = 2 * a.g;                       // 16-byte chunks per head row
   const int64_t seg = (int64_t)a.heads * row_chunks;   // chunks per gqkv segment
 
-  __shared__ __align__(16) float s_cos[TABLE ? 1 : kMaxAngles], s_sin[TABLE ? 1 : kMaxAngles];
   for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
-    const int bi = tile / a.tiles_per_batch;
+    int bi;
+    const int64_t s_base = tile_first_pos(a, tile, bi);
     const int64_t b = bi;
-    const int64_t s_base = (int64_t)(tile - bi * a.tiles_per_batch) * a.pt;
     const int64_t s = s_base + pl;
     if (!TABLE) {
-      __syncthreads();  // the previous tile's angles are no longer read
-      tile_angles(s_cos, s_sin, s_base, a.seq, a.pt, a.lg + 3, a.offset, a.head_dim, a.theta);
+      if (tile != (int)blockIdx.x) {
+        __syncthreads();  // the previous tile's angles are no longer read
+        tile_angles(s_cos, s_sin, s_base, a.seq, a.pt, a.lg + 3, a.offset, a.head_dim, a.theta);
+      }
       __syncthreads();
     }
     if (s >= a.seq) continue;

@@ -311,6 +311,8 @@ def test_throughput_vs_reference_kernels(ref_sm100a, cuda):
     dec = {
         "rope_decode_8x16x1x128_off4095": (lambda: ops.rope_embed(dq, dk, 4095, 10000.0, tab4096),
                                            lambda: ref.rope_embed(dq, dk, 4095, 10000.0)),
+        "rope_decode_in_kernel_angles_8x16x1x128_off4095": (lambda: ops.rope_embed(dq, dk, 4095, 10000.0, None),
+                                                            lambda: ref.rope_embed(dq, dk, 4095, 10000.0)),
         "embedding_decode_64_ids": (lambda: ops.embedding_lookup(ids64, tab, 45.254834, out=e64),
                                     lambda: ref.embedding_lookup(ids64, tab, e64, 45.254834)),
         "add_rms_norm_decode_64x2048": (lambda: ops.add_rms_norm(x64, b64, None, 1e-5, residual_out=r64,
