@@ -62,6 +62,25 @@ def test_rms_norm_one_wave_shape_boundary(oracle, cuda, hidden, weighted):
         assert_bits_equal(to_host(y), oracle.rms_norm(x, w, eps=1e-5), f"{rows} x {hidden}")
 
 
+@pytest.mark.parametrize("weighted", [True, False])
+def test_rms_norm_f32_two_row_shape_boundary(oracle, cuda, weighted):
+    """fp32 RMSNorm over 2048-wide rows runs 16 warps per SM (4 CTAs of 4 warps
+    at 119 registers).  A launch of one to two waves of that takes two rows per
+    warp (rows w and w + G of a grid of G warps) and so runs in one wave; below
+    and above that range a warp takes one row.  Rows at both edges of the range
+    (SMs x 16 and SMs x 32), inside it with a ragged last CTA, and past it are
+    bit-exact against the oracle."""
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    one_wave = sms * 16
+    rng = np.random.default_rng(7 + weighted)
+    w = (1 + 0.1 * rng.standard_normal(2048)).astype(np.float32) if weighted else None
+    for rows in (one_wave, one_wave + 1, one_wave + 5, sms * 24 + 3, 2 * one_wave, 2 * one_wave + 4):
+        x = rng.standard_normal((rows, 2048)).astype(np.float32)
+        dw = torch.from_numpy(w).to(cuda) if weighted else None
+        y = ops.rms_norm(torch.from_numpy(x).to(cuda), dw, eps=1e-5).cpu().numpy()
+        assert np.array_equal(y.view(np.uint32), oracle.rms_norm_f32(x, w, eps=1e-5).view(np.uint32)), rows
+
+
 def test_add_rms_norm_16384x2048(oracle, cuda):
     """Fused residual add + RMSNorm bf16 [16384 x 2048], w = 1 + 0.1 N(0,1), eps 1e-5."""
     rng = np.random.default_rng(1)
