@@ -49,6 +49,9 @@ __device__ __forceinline__ uint16_t convert_one(uint32_t bits) {
   return DTYPE == HRM_DTYPE_F32 ? loader_f32_to_bf16(bits) : loader_f32_to_bf16(f16_to_f32_bits(bits));
 }
 
+// Source loads with the default L2 priority (ld_l2): 2^28 f32 values 6.25 ->
+// 6.63 TB/s on B200 against evict-first loads; the store policy made no
+// difference, so the outputs stay evict-first.
 template <int DTYPE>
 __global__ void __launch_bounds__(kThreads) convert_vec_kernel(const uint4* src, uint4* dst, int64_t nvec) {
   grid_dependency_begin();
@@ -56,10 +59,10 @@ __global__ void __launch_bounds__(kThreads) convert_vec_kernel(const uint4* src,
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nvec; i += stride) {
     uint32_t in[8];
     if (DTYPE == HRM_DTYPE_F32) {
-      const uint4 a = ld_stream(src + 2 * i), b = ld_stream(src + 2 * i + 1);
+      const uint4 a = ld_l2(src + 2 * i), b = ld_l2(src + 2 * i + 1);
       in[0] = a.x; in[1] = a.y; in[2] = a.z; in[3] = a.w; in[4] = b.x; in[5] = b.y; in[6] = b.z; in[7] = b.w;
     } else {
-      const uint4 a = ld_stream(src + i);
+      const uint4 a = ld_l2(src + i);
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         in[2 * w] = vget(a, w) & 0xffffu;

@@ -318,6 +318,9 @@ struct SplitArgs {
   float theta;
 };
 
+// Loads and stores with the default L2 priority (ld_l2 / st_l2): 6.42 -> 6.48
+// TB/s over 65536 tokens with the cache on B200 against evict-first (the
+// stores alone with default priority measured 6.34).
 template <bool TABLE, bool CACHE>
 __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) split_rope_tile_kernel(const SplitArgs a) {
   __shared__ __align__(16) float s_cos[TABLE ? 1 : kMaxAngles], s_sin[TABLE ? 1 : kMaxAngles];
@@ -358,27 +361,27 @@ __global__ void __launch_bounds__(kThreads, HRM_ROPE_MINBLOCKS) split_rope_tile_
     const int64_t c_step = a.cache_len * row_chunks;
     for (int h = slice; h < a.heads; h += a.ht) {
       const int64_t src = in0 + (int64_t)h * row_chunks;
-      const uint4 gl = ld_stream(a.gqkv + src), gh = ld_stream(a.gqkv + src + a.g);
-      uint4 ql = ld_stream(a.gqkv + src + seg), qh = ld_stream(a.gqkv + src + seg + a.g);
-      uint4 kl = ld_stream(a.gqkv + src + 2 * seg), kh = ld_stream(a.gqkv + src + 2 * seg + a.g);
-      const uint4 vl = ld_stream(a.gqkv + src + 3 * seg), vh = ld_stream(a.gqkv + src + 3 * seg + a.g);
+      const uint4 gl = ld_l2(a.gqkv + src), gh = ld_l2(a.gqkv + src + a.g);
+      uint4 ql = ld_l2(a.gqkv + src + seg), qh = ld_l2(a.gqkv + src + seg + a.g);
+      uint4 kl = ld_l2(a.gqkv + src + 2 * seg), kh = ld_l2(a.gqkv + src + 2 * seg + a.g);
+      const uint4 vl = ld_l2(a.gqkv + src + 3 * seg), vh = ld_l2(a.gqkv + src + 3 * seg + a.g);
       rotate8<false>(ql, qh, c, sn);
       rotate8<true>(kl, kh, c, sn);
       const int64_t go = gate0 + (int64_t)h * row_chunks, o = out0 + (int64_t)h * out_step;
-      st_stream(a.gate + go, gl);
-      st_stream(a.gate + go + a.g, gh);
-      st_stream(a.q + o, ql);
-      st_stream(a.q + o + a.g, qh);
-      st_stream(a.k + o, kl);
-      st_stream(a.k + o + a.g, kh);
-      st_stream(a.v + o, vl);
-      st_stream(a.v + o + a.g, vh);
+      st_l2(a.gate + go, gl);
+      st_l2(a.gate + go + a.g, gh);
+      st_l2(a.q + o, ql);
+      st_l2(a.q + o + a.g, qh);
+      st_l2(a.k + o, kl);
+      st_l2(a.k + o + a.g, kh);
+      st_l2(a.v + o, vl);
+      st_l2(a.v + o + a.g, vh);
       if (CACHE) {
         const int64_t co = c0 + (int64_t)h * c_step;
-        st_stream(a.kc + co, kl);
-        st_stream(a.kc + co + a.g, kh);
-        st_stream(a.vc + co, vl);
-        st_stream(a.vc + co + a.g, vh);
+        st_l2(a.kc + co, kl);
+        st_l2(a.kc + co + a.g, kh);
+        st_l2(a.vc + co, vl);
+        st_l2(a.vc + co + a.g, vh);
       }
     }
   }
