@@ -65,9 +65,12 @@ namespace {
 #define HRM_RN_F32_MAXREGS HRM_RN_MAXREGS
 #endif
 // fp32 launches of one to two waves run two rows per warp in one wave (1) or
-// one row per warp (0).
+// one row per warp (0, the default).  [4096 x 2048] back to back on B200:
+// with evict-first accesses two rows per warp won (12.0 -> 11.4 us); with the
+// default-priority accesses in use now one row per warp wins (11.26 -> 11.09
+// us in-process, 5967-5992 -> 6139-6158 GB/s in bench.py).
 #ifndef HRM_RN_F32_TWO_ROWS
-#define HRM_RN_F32_TWO_ROWS 1
+#define HRM_RN_F32_TWO_ROWS 0
 #endif
 
 constexpr int kWarps = HRM_RN_WARPS;          // warp-per-row kernels
@@ -269,8 +272,7 @@ constexpr int rownorm_max_regs() {
 #define HRM_RN_PREFETCH 1
 #endif
 // Rows of a warp prefetched before the wait: its rows r and r + G of a grid of
-// G warps (one row per warp in most launches; the fp32 kernel takes two where
-// that makes its launch one wave).
+// G warps (one row per warp except in the HRM_RN_F32_TWO_ROWS build).
 constexpr int kPrefetchRows = 2;
 
 // Issues the L2 prefetches (lane 0) of this warp's first kPrefetchRows rows of
@@ -946,10 +948,9 @@ cudaError_t launch_f32_warp(const RowArgsF32& a, cudaStream_t s) {
   const int nw = warps_per_cta(a.rows, kWarps);
   int64_t blocks = (a.rows + nw - 1) / nw;
   const int64_t wave = (int64_t)device_sm_count() * o;
-  // A launch of one to two waves takes two rows per warp (rows w and w + G,
-  // both prefetched before the dependency wait), which makes it one wave:
-  // [4096 x 2048] on B200, back to back, 12.0 -> 11.4 us (1.73 -> 0.86
-  // waves).  Prefetching only the first row of the two gave 12.2 us.
+  // Option: a launch of one to two waves takes two rows per warp (rows w and
+  // w + G, both prefetched before the dependency wait), which makes it one
+  // wave (prefetching only the first row of the two was slower still).
   if (HRM_RN_F32_TWO_ROWS && blocks > wave && (blocks + 1) / 2 <= wave) blocks = (blocks + 1) / 2;
   if (HRM_RN_F32_WAVES > 0 && blocks > wave * HRM_RN_F32_WAVES) blocks = wave * HRM_RN_F32_WAVES;
   if (blocks > INT32_MAX) blocks = INT32_MAX;

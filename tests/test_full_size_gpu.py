@@ -63,13 +63,12 @@ def test_rms_norm_one_wave_shape_boundary(oracle, cuda, hidden, weighted):
 
 
 @pytest.mark.parametrize("weighted", [True, False])
-def test_rms_norm_f32_two_row_shape_boundary(oracle, cuda, weighted):
+def test_rms_norm_f32_wave_boundaries(oracle, cuda, weighted):
     """fp32 RMSNorm over 2048-wide rows runs 16 warps per SM (4 CTAs of 4 warps
-    at 119 registers).  A launch of one to two waves of that takes two rows per
-    warp (rows w and w + G of a grid of G warps) and so runs in one wave; below
-    and above that range a warp takes one row.  Rows at both edges of the range
-    (SMs x 16 and SMs x 32), inside it with a ragged last CTA, and past it are
-    bit-exact against the oracle."""
+    at 119 registers), one row per warp (the HRM_RN_F32_TWO_ROWS build takes two
+    rows per warp for launches of one to two waves).  Rows at one and two full
+    waves (SMs x 16 and SMs x 32), just past each, and between them with a
+    ragged last CTA are bit-exact against the oracle."""
     sms = torch.cuda.get_device_properties(cuda).multi_processor_count
     one_wave = sms * 16
     rng = np.random.default_rng(7 + weighted)
